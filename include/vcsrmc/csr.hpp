@@ -1,0 +1,40 @@
+// Host sparse-matrix containers and the Matrix Market loader.
+//
+// Same types, fields and behaviour as the reference's loaders:
+//   COO, read_matrix_market_coo  <- include/mmio.hpp:12-75
+//   CSR, coo_to_csr              <- include/csr.hpp:8-41
+// Errors are reported by throwing std::runtime_error, as there; the C ABI (vcsrmc.h)
+// turns them into status codes.
+#pragma once
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace vcsrmc {
+
+struct COO {
+    int M{0}, N{0};
+    std::vector<int> rows, cols;
+    std::vector<float> vals;
+};
+
+struct CSR {
+    int M{0}, N{0}, nnz{0};
+    std::vector<int> row_ptr;  // M + 1
+    std::vector<int> col;      // nnz, ascending within each row
+    std::vector<float> val;    // nnz
+};
+
+// Parses a Matrix Market "coordinate" file (real | integer | pattern; general | symmetric |
+// skew-symmetric). Indices are one-based in the file; symmetric entries are expanded; values
+// must be finite fp32; the expanded entry count must fit a signed 32-bit int.
+COO read_matrix_market_coo(const std::string& path);
+
+// Counting sort by row, then ascending columns within each row. Throws on an index out of
+// range and on a duplicate (row, column) coordinate.
+CSR coo_to_csr(const COO& coo);
+
+// Rows [r0, r1) of `csr` as a CSR of their own (row ids rebased to 0; columns unchanged).
+CSR csr_row_slice(const CSR& csr, int r0, int r1);
+
+}  // namespace vcsrmc

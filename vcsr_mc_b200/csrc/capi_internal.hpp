@@ -1,0 +1,57 @@
+// Internal definitions shared by the C ABI translation units of libvcsrmc.so.
+#pragma once
+#include <cstdint>
+#include <new>
+#include <stdexcept>
+#include <string>
+
+#include "vcsrmc.h"
+#include "vcsrmc/csr.hpp"
+#include "vcsrmc/vcsr_formats.hpp"
+
+#define VCSRMC_EXPORT extern "C" __attribute__((visibility("default")))
+
+struct vcsrmc_csr {
+    vcsrmc::CSR csr;
+};
+
+struct vcsrmc_format {
+    vcsrmc::VCSRMC v;
+};
+
+namespace vcsrmc {
+
+// Thread-local last error, reported through vcsrmc_last_error().
+void set_last_error(int status, const std::string& msg);
+int fail(int status, const std::string& msg);
+
+// An exception whose status code the C ABI returns as is.
+struct StatusError : std::runtime_error {
+    int status;
+    StatusError(int s, const std::string& m) : std::runtime_error(m), status(s) {}
+};
+
+// Runs fn() and converts exceptions into a status + last-error message.
+template <class Fn>
+int guarded(Fn&& fn) {
+    try {
+        fn();
+        return VCSRMC_OK;
+    } catch (const StatusError& e) {
+        return fail(e.status, e.what());
+    } catch (const std::bad_alloc&) {
+        return fail(VCSRMC_OOM, "host allocation failed");
+    } catch (const std::exception& e) {
+        const std::string m = e.what();
+        int s = VCSRMC_INVALID_ARG;
+        if (m.rfind("Failed to open MTX", 0) == 0) s = VCSRMC_IO_ERR;
+        else if (m.find("MTX") != std::string::npos || m.find("Duplicate") != std::string::npos ||
+                 m.find("idx out of range") != std::string::npos)
+            s = VCSRMC_FORMAT_ERR;
+        return fail(s, m);
+    } catch (...) {
+        return fail(VCSRMC_INTERNAL, "unknown exception");
+    }
+}
+
+}  // namespace vcsrmc

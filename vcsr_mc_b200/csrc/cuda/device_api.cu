@@ -1,0 +1,316 @@
+// Device half of the C ABI (vcsrmc.h): format upload/free/status, SpMM dispatch, dense
+// generator. Replaces the reference's module-global device copies and launcher
+// (src/vcsr_mc.cu:126-131, 332-404) with one handle per (format, device).
+//
+// Device layout of a format (all arrays 256-byte aligned by cudaMalloc):
+//   items  int2[n_items]    {gbeg, gend}
+//   gmeta  int4[n_groups]   {slot_begin, depth, seg_base, 0}   (one 16-byte load per group)
+//   grows  int [16*n_groups]
+//   lcol   int8[n_slots]    local column, -1 = padding (segw <= 64 fits a byte)
+//   val    fp16[n_slots] for the FP16 format (rounded to nearest even, as the reference's
+//          (_Float16) conversion), fp32[n_slots] for the FP32 format
+//   status uint32           kernel error flags (bounded waits)
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "../capi_internal.hpp"
+#include "../common/vrng.h"
+#include "../host/parallel.hpp"
+#include "common.cuh"
+#include "spmm_launch.hpp"
+
+struct vcsrmc_device_format {
+    int device = 0;
+    int M = 0, N = 0, segw = 0, fp32 = 0;
+    float scale = 1.f;
+    int64_t n_groups = 0, n_slots = 0, n_items = 0;
+    int2* items = nullptr;
+    int4* gmeta = nullptr;
+    int* grows = nullptr;
+    int8_t* lcol = nullptr;
+    void* val = nullptr;
+    uint32_t* status = nullptr;
+};
+
+namespace vcsrmc {
+namespace {
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return;
+    const int s = e == cudaErrorMemoryAllocation ? VCSRMC_OOM : VCSRMC_CUDA_ERR;
+    throw StatusError(s, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Restores the calling thread's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cuda_check(cudaGetDevice(&prev), "cudaGetDevice");
+        if (prev != dev) cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <class T>
+T* upload_array(const T* src, size_t n, cudaStream_t st) {
+    T* p = nullptr;
+    cuda_check(cudaMalloc(&p, sizeof(T) * std::max<size_t>(n, 1)), "cudaMalloc");
+    if (n) {
+        const cudaError_t e = cudaMemcpyAsync(p, src, sizeof(T) * n, cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) {
+            cudaFree(p);
+            cuda_check(e, "cudaMemcpyAsync");
+        }
+    }
+    return p;
+}
+
+void free_device(vcsrmc_device_format* d) {
+    if (!d) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(d->device);
+    cudaFree(d->items);
+    cudaFree(d->gmeta);
+    cudaFree(d->grows);
+    cudaFree(d->lcol);
+    cudaFree(d->val);
+    cudaFree(d->status);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete d;
+}
+
+// Every index the kernels dereference is checked here, once, so that a malformed format is an
+// error status instead of an out-of-bounds access on the GPU.
+void validate_format(const VCSRMC& v) {
+    const int64_t G = int64_t(v.group_depth.size());
+    const int64_t S = int64_t(v.lcol.size());
+    auto bad = [](const char* what) { throw StatusError(VCSRMC_INVALID_ARG, std::string("invalid format: ") + what); };
+    if (v.segw != 16 && v.segw != 32 && v.segw != 48 && v.segw != 64) bad("segw");
+    if (v.bundle != 16) bad("bundle");
+    if (int64_t(v.group_ptr.size()) != G + 1 || int64_t(v.group_seg_base.size()) != G ||
+        int64_t(v.group_rows.size()) != 16 * G || int64_t(v.val.size()) != S ||
+        v.item_gbeg.size() != v.item_gend.size())
+        bad("array sizes");
+    if (G * 16 > INT32_MAX || S > INT32_MAX) bad("sizes exceed 32-bit offsets");
+    if (v.group_ptr[0] != 0 || v.group_ptr[G] != S) bad("group_ptr ends");
+    for (int64_t g = 0; g < G; ++g) {
+        if (v.group_depth[g] < 0 || int64_t(v.group_ptr[g + 1]) - v.group_ptr[g] != 16 * int64_t(v.group_depth[g]))
+            bad("group_ptr/group_depth");
+        if (v.group_seg_base[g] < 0 || v.group_seg_base[g] >= std::max(v.N, 1) || v.group_seg_base[g] % v.segw)
+            bad("group_seg_base");
+    }
+    for (int64_t i = 0; i < 16 * G; ++i)
+        if (v.group_rows[i] < -1 || v.group_rows[i] >= v.M) bad("group_rows");
+    for (int64_t s = 0; s < S; ++s)
+        if (v.lcol[s] < -1 || v.lcol[s] >= v.segw) bad("lcol");
+    for (size_t i = 0; i < v.item_gbeg.size(); ++i) {
+        const int b = v.item_gbeg[i], e = v.item_gend[i];
+        if (b < 0 || e <= b || e > G) bad("item range");
+        for (int g = b + 1; g < e; ++g)
+            if (v.group_seg_base[g] != v.group_seg_base[b]) bad("item spans segments");
+    }
+}
+
+dev::DeviceFormatView view_of(const vcsrmc_device_format* d) {
+    dev::DeviceFormatView F;
+    F.items = d->items;
+    F.gmeta = d->gmeta;
+    F.grows = d->grows;
+    F.lcol = d->lcol;
+    F.val = d->val;
+    F.status = d->status;
+    F.num_items = int(d->n_items);
+    F.M = d->M;
+    F.N = d->N;
+    F.segw = d->segw;
+    F.scale = d->scale;
+    return F;
+}
+
+void check_spmm_args(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb, int32_t O,
+                     int32_t tileK, const float* C, int64_t ldc) {
+    if (!d) throw StatusError(VCSRMC_INVALID_ARG, "NULL format");
+    if (O < 1) throw StatusError(VCSRMC_INVALID_ARG, "O must be >= 1");
+    if (tileK != 16 && tileK != 32 && tileK != 64 && tileK != 128 && tileK != 256)
+        throw StatusError(VCSRMC_INVALID_ARG, "tileK must be one of 16, 32, 64, 128, 256");
+    if (b_dtype != VCSRMC_F32 && b_dtype != VCSRMC_F16) throw StatusError(VCSRMC_INVALID_ARG, "unknown B dtype");
+    if (b_dtype == VCSRMC_F16 && d->fp32)
+        throw StatusError(VCSRMC_INVALID_ARG, "the FP32 format takes fp32 B only");
+    if (ldb < O || ldc < O) throw StatusError(VCSRMC_INVALID_ARG, "ldb and ldc must be >= O");
+    if ((d->N > 0 && !B) || (d->M > 0 && !C)) throw StatusError(VCSRMC_INVALID_ARG, "NULL B or C");
+}
+
+void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb, int32_t O, int32_t tileK,
+                 float* C, int64_t ldc, int accumulate, cudaStream_t st) {
+    if (!accumulate && d->M > 0) {
+        if (ldc == O)
+            cuda_check(cudaMemsetAsync(C, 0, sizeof(float) * size_t(d->M) * size_t(O), st), "cudaMemsetAsync");
+        else
+            cuda_check(cudaMemset2DAsync(C, size_t(ldc) * sizeof(float), 0, size_t(O) * sizeof(float), size_t(d->M), st),
+                       "cudaMemset2DAsync");
+    }
+    const dev::DeviceFormatView F = view_of(d);
+    cudaError_t e;
+    if (d->fp32)
+        e = dev::spmm_fp32_atomic(F, static_cast<const float*>(B), ldb, O, tileK, C, ldc, st);
+    else
+        e = dev::spmm_fp16_tc_atomic(F, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, tileK, C, ldc, st);
+    cuda_check(e, "SpMM launch");
+}
+
+__global__ void gen_dense_kernel(int64_t rows, int cols, uint64_t key, int f16, void* out, int64_t ld) {
+    const int64_t total = rows * int64_t(cols);
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = i / cols, c = i % cols;
+        const float v = vrng_sym(vrng_at(key, uint64_t(i)));
+        if (f16)
+            static_cast<__half*>(out)[r * ld + c] = __float2half_rn(v);
+        else
+            static_cast<float*>(out)[r * ld + c] = v;
+    }
+}
+
+}  // namespace
+
+namespace dev {
+cudaError_t gen_dense_device(int64_t rows, int cols, uint64_t seed, int f16, void* out, int64_t ld, cudaStream_t st) {
+    const int64_t total = rows * int64_t(cols);
+    if (total == 0) return cudaSuccess;
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, int64_t(sms) * 16);
+    gen_dense_kernel<<<unsigned(blocks), 256, 0, st>>>(rows, cols, vrng_key(seed, VRNG_STREAM_DENSE), f16, out, ld);
+    return cudaGetLastError();
+}
+}  // namespace dev
+
+}  // namespace vcsrmc
+
+using namespace vcsrmc;
+
+VCSRMC_EXPORT int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out) {
+    return guarded([&] {
+        if (!f || !out) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        const VCSRMC& v = f->v;
+        validate_format(v);
+        DeviceGuard guard(device);
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        auto* d = new vcsrmc_device_format;
+        d->device = device;
+        d->M = v.M;
+        d->N = v.N;
+        d->segw = v.segw;
+        d->fp32 = v.fp32 ? 1 : 0;
+        d->scale = v.scale;
+        d->n_groups = int64_t(v.group_depth.size());
+        d->n_slots = int64_t(v.lcol.size());
+        d->n_items = int64_t(v.item_gbeg.size());
+        try {
+            const int64_t G = d->n_groups, S = d->n_slots, I = d->n_items;
+            const int nth = resolve_threads(0);
+            std::vector<int2> items(I);
+            for (int64_t i = 0; i < I; ++i) items[i] = make_int2(v.item_gbeg[i], v.item_gend[i]);
+            std::vector<int4> gmeta(G);
+            for (int64_t g = 0; g < G; ++g)
+                gmeta[g] = make_int4(v.group_ptr[g], v.group_depth[g], v.group_seg_base[g], 0);
+            std::vector<int8_t> lcol(S);
+            parallel_for(0, S, nth, [&](int64_t a, int64_t b) {
+                for (int64_t s = a; s < b; ++s) lcol[s] = int8_t(v.lcol[s]);
+            });
+            d->items = upload_array(items.data(), items.size(), st);
+            d->gmeta = upload_array(gmeta.data(), gmeta.size(), st);
+            d->grows = upload_array(v.group_rows.data(), v.group_rows.size(), st);
+            d->lcol = upload_array(lcol.data(), lcol.size(), st);
+            if (d->fp32) {
+                d->val = upload_array(v.val.data(), v.val.size(), st);
+            } else {
+                std::vector<__half> h(S);
+                parallel_for(0, S, nth, [&](int64_t a, int64_t b) {
+                    for (int64_t s = a; s < b; ++s) h[s] = __float2half_rn(v.val[s]);
+                });
+                d->val = upload_array(h.data(), h.size(), st);
+                cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+            }
+            cuda_check(cudaMalloc(&d->status, sizeof(uint32_t)), "cudaMalloc");
+            cuda_check(cudaMemsetAsync(d->status, 0, sizeof(uint32_t), st), "cudaMemsetAsync");
+            cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        } catch (...) {
+            free_device(d);
+            throw;
+        }
+        *out = d;
+    });
+}
+
+VCSRMC_EXPORT int vcsrmc_device_free(vcsrmc_device_format* d) {
+    return guarded([&] { free_device(d); });
+}
+
+VCSRMC_EXPORT int vcsrmc_device_status(const vcsrmc_device_format* d, uint32_t* flags, int clear) {
+    return guarded([&] {
+        if (!d || !flags) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        DeviceGuard guard(d->device);
+        cuda_check(cudaMemcpy(flags, d->status, sizeof(uint32_t), cudaMemcpyDeviceToHost), "cudaMemcpy");
+        if (clear) cuda_check(cudaMemset(d->status, 0, sizeof(uint32_t)), "cudaMemset");
+    });
+}
+
+VCSRMC_EXPORT int vcsrmc_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb, int32_t O,
+                              int32_t tileK, float* C, int64_t ldc, int accumulate, void* stream) {
+    return guarded([&] {
+        check_spmm_args(d, B, b_dtype, ldb, O, tileK, C, ldc);
+        DeviceGuard guard(d->device);
+        launch_spmm(d, B, b_dtype, ldb, O, tileK, C, ldc, accumulate, static_cast<cudaStream_t>(stream));
+    });
+}
+
+VCSRMC_EXPORT int vcsrmc_spmm_timed(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb,
+                                    int32_t O, int32_t tileK, float* C, int64_t ldc, int accumulate, void* stream,
+                                    float* ms) {
+    return guarded([&] {
+        if (!ms) throw StatusError(VCSRMC_INVALID_ARG, "NULL ms");
+        check_spmm_args(d, B, b_dtype, ldb, O, tileK, C, ldc);
+        DeviceGuard guard(d->device);
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        cudaEvent_t t0 = nullptr, t1 = nullptr;
+        cuda_check(cudaEventCreate(&t0), "cudaEventCreate");
+        cudaError_t e = cudaEventCreate(&t1);
+        if (e != cudaSuccess) { cudaEventDestroy(t0); cuda_check(e, "cudaEventCreate"); }
+        try {
+            cuda_check(cudaEventRecord(t0, st), "cudaEventRecord");
+            launch_spmm(d, B, b_dtype, ldb, O, tileK, C, ldc, accumulate, st);
+            cuda_check(cudaEventRecord(t1, st), "cudaEventRecord");
+            cuda_check(cudaEventSynchronize(t1), "cudaEventSynchronize");
+            cuda_check(cudaEventElapsedTime(ms, t0, t1), "cudaEventElapsedTime");
+        } catch (...) {
+            cudaEventDestroy(t0);
+            cudaEventDestroy(t1);
+            throw;
+        }
+        cudaEventDestroy(t0);
+        cudaEventDestroy(t1);
+        uint32_t flags = 0;
+        cuda_check(cudaMemcpy(&flags, d->status, sizeof(uint32_t), cudaMemcpyDeviceToHost), "cudaMemcpy");
+        if (flags & dev::kStatusTimeout) throw StatusError(VCSRMC_TIMEOUT, "a bounded device wait expired");
+    });
+}
+
+VCSRMC_EXPORT int vcsrmc_gen_dense_device(int64_t rows, int32_t cols, uint64_t seed, int dtype, void* out,
+                                          int64_t ld, void* stream) {
+    return guarded([&] {
+        if (rows < 0 || cols <= 0 || ld < cols || (rows && !out) || (dtype != VCSRMC_F32 && dtype != VCSRMC_F16))
+            throw StatusError(VCSRMC_INVALID_ARG, "bad dense arguments");
+        cuda_check(dev::gen_dense_device(rows, cols, seed, dtype == VCSRMC_F16 ? 1 : 0, out, ld,
+                                         static_cast<cudaStream_t>(stream)),
+                   "gen_dense_device");
+    });
+}
