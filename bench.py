@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""VCSR-MC SpMM benchmark (one JSON line on rank 0).
+
+Default workload: BASELINE config 4, the one the 1/2/4/8-GPU metric and the north_star roofline
+target are quoted on: R-MAT A with 2^24 rows/cols (2^28 samples, (a,b,c) = (.57,.19,.19),
+duplicates removed, ~261M nnz, values U(-1,1)), B 2^24 x 128 fp16 U(-1,1), C fp32, FP16 path
+(tcgen05), segw 32, tileK 128. Synthetic, seeded inputs (seed 0) stand in for the dataset.
+
+A step = C = A*B over the whole matrix: zero C, then one VCSR-MC SpMM launch (C += A*B, the
+reference's contract). With --gpus P (torchrun, one rank per GPU) A is cut into P nnz-balanced
+row blocks, B is replicated, each rank owns its rows of C; there is no collective on the data
+path (strong scaling: the total work is fixed). Time = max over ranks of the device time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload rmat|c1|c2|c3] [--dtype fp16|fp32]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+O_COLS = 128
+SEED = 0
+CACHE_DIR = os.environ.get("VCSRMC_BENCH_CACHE", "/dev/shm/vcsrmc_bench")
+
+
+def log(msg: str) -> None:
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(f"[bench] {msg}", file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------------------------
+def workload_spec(name: str, scale: int) -> dict:
+    import vcsr_mc_b200 as vm
+    if name == "rmat":
+        return {"kind": vm.GEN_RMAT, "param": scale,
+                "desc": f"config4 R-MAT 2^{scale} rows, 2^{scale + 4} samples (a,b,c)=(0.57,0.19,0.19), dedup"}
+    if name == "c1":
+        return {"kind": vm.GEN_UNIFORM_POISSON, "param": 4096, "desc": "config1 4096^2 Poisson(16)"}
+    if name == "c2":
+        return {"kind": vm.GEN_ZIPF, "param": 262144, "desc": "config2 262144^2 Zipf(1.8) mean 10 cap 8192"}
+    if name == "c3":
+        return {"kind": vm.GEN_STENCIL27, "param": 100, "desc": "config3 27-point stencil 100^3"}
+    raise SystemExit(f"unknown workload {name}")
+
+
+def load_or_generate_csr(spec: dict, rank: int, world: int, dist_barrier) -> tuple:
+    """Rank 0 generates the CSR (all host threads) into a shared-memory cache; all ranks load it."""
+    import vcsr_mc_b200 as vm
+    key = f"k{spec['kind']}_p{spec['param']}_s{SEED}"
+    d = os.path.join(CACHE_DIR, key)
+    done = os.path.join(d, "done")
+    if rank == 0 and not os.path.exists(done):
+        t = time.time()
+        A = vm.CSR.generate(spec["kind"], spec["param"], seed=SEED)
+        rp, col, val = A.arrays(copy=False)
+        try:
+            os.makedirs(d, exist_ok=True)
+            np.save(os.path.join(d, "row_ptr.npy"), rp)
+            np.save(os.path.join(d, "col.npy"), col)
+            np.save(os.path.join(d, "val.npy"), val)
+            with open(os.path.join(d, "meta.json"), "w") as f:
+                json.dump({"M": A.M, "N": A.N, "nnz": A.nnz}, f)
+            open(done, "w").close()
+            cached = True
+        except OSError:
+            cached = False
+        log(f"generated {spec['desc']}: nnz={A.nnz} in {time.time() - t:.1f}s (cached={cached})")
+        if world == 1 or not cached:
+            if world > 1:
+                raise SystemExit("multi-rank runs need the shared CSR cache")
+            return A.M, A.N, np.array(rp), np.array(col), np.array(val)
+    dist_barrier()
+    with open(os.path.join(d, "meta.json")) as f:
+        meta = json.load(f)
+    rp = np.load(os.path.join(d, "row_ptr.npy"), mmap_mode="r")
+    col = np.load(os.path.join(d, "col.npy"), mmap_mode="r")
+    val = np.load(os.path.join(d, "val.npy"), mmap_mode="r")
+    return meta["M"], meta["N"], rp, col, val
+
+
+def algorithmic_bytes(nnz: int, M: int, D: int, O: int, s_ab: int) -> int:
+    """Compulsory bytes of one SpMM: A (col int32 + value), row_ptr, the D distinct rows of B
+    that A touches, and C (fp32) written once."""
+    return nnz * (4 + s_ab) + (M + 1) * 4 + D * O * s_ab + M * O * 4
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks (sampled with nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baselines (the reference's own fp64 CSR loop, src/main.cpp:202-207, from oracle/_ref)
+# ---------------------------------------------------------------------------------------------
+def cpu_sample(M, N, rp, col, val, target_nnz: int):
+    """Every k-th row of A (k chosen for ~target_nnz), columns compacted to the rows of B they
+    touch. Returns (row_ptr, col, val, B_compact, description)."""
+    nnz = int(rp[M])
+    k = max(1, int(round(nnz / max(1, target_nnz))))
+    rows = np.arange(0, M, k, dtype=np.int64)
+    starts, ends = np.asarray(rp[rows], dtype=np.int64), np.asarray(rp[rows + 1], dtype=np.int64)
+    lens = ends - starts
+    srp = np.zeros(rows.size + 1, dtype=np.int64)
+    np.cumsum(lens, out=srp[1:])
+    idx = np.repeat(starts - srp[:-1], lens) + np.arange(srp[-1])
+    scol = np.asarray(col)[idx]
+    sval = np.asarray(val)[idx].astype(np.float32)
+    uniq, inv = np.unique(scol, return_inverse=True)
+    from vcsr_mc_b200 import rng
+    Bfull_rows = np.empty((uniq.size, O_COLS), dtype=np.float32)
+    for s in range(0, uniq.size, 1 << 16):  # rows of the dense stream = the GPU's B values
+        Bfull_rows[s:s + (1 << 16)] = rng.dense_rows(uniq[s:s + (1 << 16)], O_COLS, SEED)
+    desc = (f"every {k}-th row of A ({rows.size} rows, {int(srp[-1])} nnz), B compacted to the "
+            f"{uniq.size} rows those touch, fp32, O={O_COLS}")
+    return srp.astype(np.int32), inv.astype(np.int32), sval, Bfull_rows, desc, int(srp[-1])
+
+
+def time_reference_cpu(M, N, rp, col, val, steps: int, warmup: int, target_nnz: int, fp16_b: bool):
+    from oracle import bind as ob
+    if not ob.ref_available():
+        raise RuntimeError("oracle/_ref/libvcsr_ref.so not built")
+    srp, scol, sval, Bs, desc, snnz = cpu_sample(M, N, rp, col, val, target_nnz)
+    if fp16_b:
+        Bs = Bs.astype(np.float16).astype(np.float32)
+    cores = len(os.sched_getaffinity(0))
+    runner = ob.RefSpmm(srp, scol, sval, Bs, nslices=cores)
+    for _ in range(warmup):
+        runner.run()
+    t = time.perf_counter()
+    for _ in range(steps):
+        runner.run()
+    dt = (time.perf_counter() - t) / max(1, steps)
+    runner.close()
+    return {"value": 2.0 * snnz * O_COLS / dt / 1e9, "unit": "GFLOP/s", "cores": cores, "kind": "reference",
+            "sample": desc + f"; reference loop src/main.cpp:202-207 on {cores} row slices/threads",
+            "ms_per_step": dt * 1e3}
+
+
+# ---------------------------------------------------------------------------------------------
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["rmat", "c1", "c2", "c3"], default="rmat")
+    ap.add_argument("--scale", type=int, default=24)
+    ap.add_argument("--dtype", choices=["fp16", "fp32"], default="fp16")
+    ap.add_argument("--segw", type=int, default=32)
+    ap.add_argument("--tileK", type=int, default=128)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-nnz", type=int, default=8_000_000)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    spec = workload_spec(args.workload, args.scale)
+    fp16 = args.dtype == "fp16"
+    config = {"workload": spec["desc"], "O": O_COLS, "segw": args.segw, "tileK": args.tileK,
+              "path": "fp16 tcgen05" if fp16 else "fp32 ffma", "plan": "vcsr-mc item/segment-major, C reductions",
+              "parallelism": f"row-shard x{args.gpus} (nnz-balanced), B replicated",
+              "l2": "inputs larger than L2 (no flush needed)"}
+
+    if args.impl == "reference":
+        # The reference's own CPU implementation of the path (oracle/_ref), rank 0 only.
+        if rank != 0:
+            return
+        try:
+            M, N, rp, col, val = load_or_generate_csr(spec, 0, 1, lambda: None)
+            cb = time_reference_cpu(M, N, rp, col, val, args.steps, args.warmup, args.cpu_sample_nnz, fp16)
+        except Exception as e:  # noqa: BLE001
+            print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"}))
+            return
+        print(json.dumps({
+            "impl": "reference", "metric": "SpMM effective GFLOP/s (2*nnz*N/t)", "value": cb["value"],
+            "unit": "GFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f64" , "data": "synthetic", "config": config,
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+    import vcsr_mc_b200 as vm
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist  # noqa: F811
+        dist.init_process_group("nccl", timeout=datetime.timedelta(minutes=20), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    cores = len(os.sched_getaffinity(0))
+    t0 = time.time()
+    M, N, rp, col, val = load_or_generate_csr(spec, rank, world, barrier)
+    nnz_total = int(rp[M])
+    cuts = vm.partition_rows(np.asarray(rp, dtype=np.int32), world)
+    r0, r1 = int(cuts[rank]), int(cuts[rank + 1])
+    p0, p1 = int(rp[r0]), int(rp[r1])
+    shard = vm.CSR.from_arrays(r1 - r0, N, np.asarray(rp[r0:r1 + 1], dtype=np.int64) - p0,
+                               np.asarray(col[p0:p1]), np.asarray(val[p0:p1]))
+    nthreads = max(1, cores // world)
+    tb = time.time()
+    V = vm.csr_to_vcsr_mc(shard, fp32=not fp16, segw=args.segw, nthreads=nthreads)
+    build_s = time.time() - tb
+    D = int(np.unique(np.asarray(col[p0:p1])).size) if p1 > p0 else 0
+    dV = vm.upload_vcsr_mc_device(V, device=local)
+    Ms = r1 - r0
+    groups, slots, items = V.n_groups, V.n_slots, V.n_items
+    del V
+    log(f"rank {rank}: rows [{r0},{r1}) nnz {p1 - p0} groups {groups} slots {slots} items {items} "
+        f"build {build_s:.1f}s setup {time.time() - t0:.1f}s")
+
+    dt = torch.float16 if fp16 else torch.float32
+    B = torch.empty((N, O_COLS), dtype=dt, device="cuda")
+    vm.gen_dense_device(B, SEED)
+    C = torch.empty((max(Ms, 1), O_COLS), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(ev_k0=None, ev_k1=None):
+        C.zero_()
+        if ev_k0 is not None:
+            ev_k0.record(stream)
+        vm.spmm(dV, B, C, tileK=args.tileK, accumulate=True, stream=stream)
+        if ev_k1 is not None:
+            ev_k1.record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(args.steps):
+        step(*kev[i])
+    stop.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    total_ms = start.elapsed_time(stop)
+    kern_ms = float(np.mean([a.elapsed_time(b) for a, b in kev]))
+    status = dV.status()
+    # max over ranks
+    t = torch.tensor([total_ms, kern_ms], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, kern_max_ms = float(t[0]), float(t[1])
+    ms_per_step = total_ms / args.steps
+    flops = 2.0 * nnz_total * O_COLS
+    value = flops / (ms_per_step * 1e-3) / 1e9
+
+    # roofline of the SpMM kernel on this rank (algorithmic bytes of this rank's launch)
+    s_ab = 2 if fp16 else 4
+    bytes_alg = algorithmic_bytes(p1 - p0, Ms, D, O_COLS, s_ab)
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, peak_src = 6650.0, "fallback 6.65 TB/s"
+    if os.path.exists(peaks_path):
+        with open(peaks_path) as f:
+            peak = float(json.load(f)["hbm_gbs"])
+        peak_src = "measured (MEASURED_PEAKS.json hbm_gbs)"
+    achieved = bytes_alg / (kern_ms * 1e-3) / 1e9
+
+    # end to end through the C ABI with host buffers: H2D of B (pinned), zero C, SpMM, D2H of C
+    e2e = None
+    if not args.no_e2e and args.e2e_steps > 0:
+        hB = B.cpu().pin_memory()
+        hC = torch.empty(C.shape, dtype=torch.float32).pin_memory()
+        for i in range(args.e2e_steps + 1):
+            if i == 1:
+                barrier()
+                torch.cuda.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            B.copy_(hB, non_blocking=True)
+            C.zero_()
+            vm.spmm(dV, B, C, tileK=args.tileK, accumulate=True, stream=stream)
+            hC.copy_(C, non_blocking=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], dtype=torch.float64, device="cuda")
+        if dist is not None:
+            dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": flops / (float(e2e_ms) * 1e-3) / 1e9, "unit": "GFLOP/s",
+               "h2d_bytes_per_step": int(hB.numel() * hB.element_size()),
+               "d2h_bytes_per_step": int(hC.numel() * hC.element_size()), "ms_per_step": float(e2e_ms)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cb = time_reference_cpu(M, N, rp, col, val, 3, 1, args.cpu_sample_nnz, fp16)
+            cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        except Exception as e:  # noqa: BLE001
+            cpu = {"value": None, "unavailable": f"{type(e).__name__}: {e}"}
+
+    if rank == 0:
+        line = {
+            "metric": "SpMM effective GFLOP/s (2*nnz*N/t)", "value": value, "unit": "GFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16" if fp16 else "f32",
+            "data": "synthetic (seeded generator, seed 0)",
+            "config": config,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                         "kernel": "vcsr_mc_fp16_tc_kernel" if fp16 else "vcsr_mc_fp32_kernel",
+                         "kernel_ms": kern_ms, "kernel_ms_max_over_ranks": kern_max_ms,
+                         "algorithmic_bytes": bytes_alg},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+            "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+            "detail": {"nnz": nnz_total, "M": M, "N": N, "rank0_rows": Ms, "rank0_distinct_cols": D,
+                       "groups": groups, "slots": slots, "items": items, "device_status": status,
+                       "clock_samples": clk["samples"]},
+        }
+        print(json.dumps(line), flush=True)
+    dV.free()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
