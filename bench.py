@@ -213,6 +213,7 @@ def main() -> None:
     ap.add_argument("--dtype", choices=["fp16", "fp32"], default="fp16")
     ap.add_argument("--segw", type=int, default=32)
     ap.add_argument("--tileK", type=int, default=128)
+    ap.add_argument("--plan", choices=["rows", "segment"], default="rows")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -226,7 +227,9 @@ def main() -> None:
     spec = workload_spec(args.workload, args.scale)
     fp16 = args.dtype == "fp16"
     config = {"workload": spec["desc"], "O": O_COLS, "segw": args.segw, "tileK": args.tileK,
-              "path": "fp16 tcgen05" if fp16 else "fp32 ffma", "plan": "vcsr-mc item/segment-major, C reductions",
+              "path": (("fp16 A/B, fp32 accumulate, " if fp16 else "fp32, ") +
+                       ("CUDA-core FFMA" if (args.plan == "rows" or not fp16) else "tcgen05 MMA, TMEM accumulator")), "plan": {"rows": "rows: row-stationary over the VCSR-MC row view, C stored once",
+                       "segment": "segment: reference dataflow, per-item B segment, C reductions"}[args.plan],
               "parallelism": f"row-shard x{args.gpus} (nnz-balanced), B replicated",
               "l2": "inputs larger than L2 (no flush needed)"}
 
@@ -277,7 +280,8 @@ def main() -> None:
     V = vm.csr_to_vcsr_mc(shard, fp32=not fp16, segw=args.segw, nthreads=nthreads)
     build_s = time.time() - tb
     D = int(np.unique(np.asarray(col[p0:p1])).size) if p1 > p0 else 0
-    dV = vm.upload_vcsr_mc_device(V, device=local)
+    plan = vm.PLAN_ROWS if args.plan == "rows" else vm.PLAN_SEGMENT
+    dV = vm.upload_vcsr_mc_device(V, device=local, plans=[plan])
     Ms = r1 - r0
     groups, slots, items = V.n_groups, V.n_slots, V.n_items
     del V
@@ -291,10 +295,13 @@ def main() -> None:
     stream = torch.cuda.current_stream()
 
     def step(ev_k0=None, ev_k1=None):
-        C.zero_()
+        # ROWS plan: every C row is stored once, so no zeroing pass; SEGMENT plan: C += A*B
+        # through reductions needs C zeroed first (the reference's caller does the same).
+        if plan == vm.PLAN_SEGMENT:
+            C.zero_()
         if ev_k0 is not None:
             ev_k0.record(stream)
-        vm.spmm(dV, B, C, tileK=args.tileK, accumulate=True, stream=stream)
+        vm.spmm(dV, B, C, tileK=args.tileK, accumulate=plan == vm.PLAN_SEGMENT, stream=stream, plan=plan)
         if ev_k1 is not None:
             ev_k1.record(stream)
 
@@ -350,8 +357,9 @@ def main() -> None:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
             B.copy_(hB, non_blocking=True)
-            C.zero_()
-            vm.spmm(dV, B, C, tileK=args.tileK, accumulate=True, stream=stream)
+            if plan == vm.PLAN_SEGMENT:
+                C.zero_()
+            vm.spmm(dV, B, C, tileK=args.tileK, accumulate=plan == vm.PLAN_SEGMENT, stream=stream, plan=plan)
             hC.copy_(C, non_blocking=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e1.record(stream)
@@ -380,10 +388,11 @@ def main() -> None:
             "config": config,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
-                         "kernel": "vcsr_mc_fp16_tc_kernel" if fp16 else "vcsr_mc_fp32_kernel",
+                         "kernel": ("vcsr_rows_kernel" if args.plan == "rows" else
+                                    "vcsr_mc_fp16_tc_kernel" if fp16 else "vcsr_mc_fp32_kernel"),
                          "kernel_ms": kern_ms, "kernel_ms_max_over_ranks": kern_max_ms,
                          "algorithmic_bytes": bytes_alg},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps * (2 if args.plan == "rows" else 1),
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "detail": {"nnz": nnz_total, "M": M, "N": N, "rank0_rows": Ms, "rank0_distinct_cols": D,
                        "groups": groups, "slots": slots, "items": items, "device_status": status,

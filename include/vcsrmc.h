@@ -42,6 +42,16 @@ extern "C" {
 #define VCSRMC_F32 0
 #define VCSRMC_F16 1
 
+/* ---- execution plans (vcsrmc_upload_ex / vcsrmc_spmm_ex) ------------------------------
+ * SEGMENT: the reference's dataflow (src/vcsr_mc.cu:143-329): per work item, stage the B
+ *          segment once, multiply every 16-row group, add it into C with reductions.
+ * ROWS:    row-stationary over the format's row view (built at upload): each C row is
+ *          accumulated in registers from gathered B rows and stored once.
+ * AUTO:    ROWS when its layout is resident, else SEGMENT.                                */
+#define VCSRMC_PLAN_AUTO 0
+#define VCSRMC_PLAN_SEGMENT 1
+#define VCSRMC_PLAN_ROWS 2
+
 /* ---- synthetic configurations (vcsrmc_gen_csr) ---------------------------------------- */
 #define VCSRMC_GEN_UNIFORM_POISSON 1 /* param: M = N; mean row length 16                   */
 #define VCSRMC_GEN_ZIPF 2            /* param: M = N; Zipf(1.8) lengths, mean 10, cap 8192  */
@@ -116,6 +126,10 @@ void vcsrmc_format_free(vcsrmc_format* f);
 /* Validates the format's index arrays on the host, then copies them to `device` in the
  * kernels' layout (FP16 formats keep fp16 values on the device). Blocking. */
 int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out);
+/* Same, choosing which plan layouts to make resident: a bit mask of (1 << VCSRMC_PLAN_SEGMENT)
+ * and (1 << VCSRMC_PLAN_ROWS); 0 = all (what vcsrmc_upload does). */
+int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans, void* stream,
+                     vcsrmc_device_format** out);
 int vcsrmc_device_free(vcsrmc_device_format* d);
 /* Error flags raised by kernels of this format since the last clear (bit 0: a bounded wait
  * timed out). Blocking read. */
@@ -130,6 +144,10 @@ int vcsrmc_device_status(const vcsrmc_device_format* d, uint32_t* flags, int cle
  * Asynchronous on `stream`. */
 int vcsrmc_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb, int32_t O,
                 int32_t tileK, float* C, int64_t ldc, int accumulate, void* stream);
+/* Same, with an explicit plan (VCSRMC_PLAN_*); the plan's layout must be resident. */
+int vcsrmc_spmm_ex(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb,
+                   int32_t O, int32_t tileK, float* C, int64_t ldc, int accumulate, int plan,
+                   void* stream);
 /* Blocking form with the reference's semantics: records events around the launch, waits,
  * returns the elapsed milliseconds in *ms (src/vcsr_mc.cu:380-393). */
 int vcsrmc_spmm_timed(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb,

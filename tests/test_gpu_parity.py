@@ -15,21 +15,24 @@ from tests.helpers import check_fp16, check_fp32, random_csr
 pytestmark = pytest.mark.gpu
 
 
+PLANS = [vm.PLAN_SEGMENT, vm.PLAN_ROWS]
+PLAN_IDS = ["segment", "rows"]
+
+
 def run_gpu(torch, A: vm.CSR, B32: np.ndarray, fp32: bool, segw: int, tileK: int, b_half: bool,
-            accumulate_into=None, ldb_pad: int = 0, ldc_pad: int = 0):
-    """C = A*B (or C = accumulate_into + A*B) on cuda:0; returns (C, B values actually used)."""
+            accumulate_into=None, ldb_pad: int = 0, ldc_pad: int = 0, plan: int = vm.PLAN_SEGMENT):
+    """C = A*B (or C = accumulate_into + A*B) on cuda:0 with one plan; returns (C, B values used)."""
     O = B32.shape[1]
     V = vm.csr_to_vcsr_mc(A, fp32=fp32, segw=segw)
-    dV = vm.upload_vcsr_mc_device(V, device=0)
+    dV = vm.upload_vcsr_mc_device(V, device=0, plans=[plan])
     dt = torch.float16 if b_half else torch.float32
     Bfull = torch.zeros((B32.shape[0], O + ldb_pad), dtype=dt, device="cuda")
     Bfull[:, :O] = torch.from_numpy(B32).to(device="cuda", dtype=dt)
-    Cfull = torch.zeros((A.M, O + ldc_pad), dtype=torch.float32, device="cuda")
+    Cfull = torch.full((A.M, O + ldc_pad), 7.0, dtype=torch.float32, device="cuda")
     if accumulate_into is not None:
         Cfull[:, :O] = torch.from_numpy(accumulate_into).cuda()
-    ms = vm.run_vcsr_mc_spmm_gpu(dV, Bfull, O, tileK, Cfull, accumulate=accumulate_into is not None)
+    vm.spmm(dV, Bfull, Cfull, tileK=tileK, accumulate=accumulate_into is not None, O=O, plan=plan)
     torch.cuda.synchronize()
-    assert ms >= 0.0
     assert dV.status() == 0, "a bounded device wait expired"
     C = Cfull[:, :O].cpu().numpy()
     Bused = Bfull[:, :O].float().cpu().numpy()
@@ -48,112 +51,124 @@ def oracle_check(A: vm.CSR, C, Bused, fp32: bool, base=None):
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
 @pytest.mark.parametrize("segw", [16, 32, 48, 64])
-def test_config1_segw(cuda, fp32, segw):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_config1_segw(cuda, plan, fp32, segw):
     A = vm.CSR.generate(vm.GEN_UNIFORM_POISSON, 4096, seed=0)
     B = vm.gen_dense_host(4096, 128, seed=0)
-    C, Bu = run_gpu(cuda, A, B, fp32, segw, 128, b_half=not fp32)
+    C, Bu = run_gpu(cuda, A, B, fp32, segw, 128, b_half=not fp32, plan=plan)
     oracle_check(A, C, Bu, fp32)
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
 @pytest.mark.parametrize("tileK", [16, 32, 64, 128, 256])
-def test_config1_tilek(cuda, fp32, tileK):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_config1_tilek(cuda, plan, fp32, tileK):
     A = vm.CSR.generate(vm.GEN_UNIFORM_POISSON, 4096, seed=0)
     B = vm.gen_dense_host(4096, 256, seed=1)
-    C, Bu = run_gpu(cuda, A, B, fp32, 32, tileK, b_half=not fp32)
+    C, Bu = run_gpu(cuda, A, B, fp32, 32, tileK, b_half=not fp32, plan=plan)
     oracle_check(A, C, Bu, fp32)
 
 
-def test_fp16_with_fp32_b(cuda):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_fp16_with_fp32_b(cuda, plan):
     """The reference's FP16 kernel reads fp32 B and converts it (src/vcsr_mc.cu:184-196)."""
     A = vm.CSR.generate(vm.GEN_UNIFORM_POISSON, 4096, seed=3)
     B = vm.gen_dense_host(4096, 128, seed=3)
-    C, _ = run_gpu(cuda, A, B, False, 32, 128, b_half=False)
+    C, _ = run_gpu(cuda, A, B, False, 32, 128, b_half=False, plan=plan)
     Bh = B.astype(np.float16).astype(np.float32)  # the values the tensor cores multiply
     oracle_check(A, C, Bh, False)
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
-def test_zipf_power_law(cuda, fp32):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_zipf_power_law(cuda, plan, fp32):
     A = vm.CSR.generate(vm.GEN_ZIPF, 1 << 16, seed=0)
     B = vm.gen_dense_host(1 << 16, 128, seed=0)
-    C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32)
+    C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32, plan=plan)
     oracle_check(A, C, Bu, fp32)
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
-def test_stencil27(cuda, fp32):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_stencil27(cuda, plan, fp32):
     A = vm.CSR.generate(vm.GEN_STENCIL27, 24, seed=0)
     B = vm.gen_dense_host(A.N, 128, seed=0)
-    C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32)
+    C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32, plan=plan)
     oracle_check(A, C, Bu, fp32)
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
-def test_rmat_small(cuda, fp32):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_rmat_small(cuda, plan, fp32):
     A = vm.CSR.generate(vm.GEN_RMAT, 14, seed=0)
     B = vm.gen_dense_host(A.N, 128, seed=0)
-    C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32)
+    C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32, plan=plan)
     oracle_check(A, C, Bu, fp32)
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
 @pytest.mark.parametrize("O", [1, 7, 40, 100, 130])
-def test_ragged_width(cuda, fp32, O):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_ragged_width(cuda, plan, fp32, O):
     """O not a multiple of 4, of 16 or of the slab; O < 64 takes the non-TMA staging path."""
     rp, col, val = random_csr(301, 777, 0.02, seed=O)
     A = vm.CSR.from_arrays(301, 777, rp, col, val)
     B = np.random.default_rng(O).uniform(-1, 1, size=(777, O)).astype(np.float32)
-    C, Bu = run_gpu(cuda, A, B, fp32, 32, 64, b_half=not fp32)
+    C, Bu = run_gpu(cuda, A, B, fp32, 32, 64, b_half=not fp32, plan=plan)
     oracle_check(A, C, Bu, fp32)
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
-def test_strided_b_and_c(cuda, fp32):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_strided_b_and_c(cuda, plan, fp32):
     rp, col, val = random_csr(200, 300, 0.05, seed=5, empty_rows=True)
     A = vm.CSR.from_arrays(200, 300, rp, col, val)
     B = np.random.default_rng(5).uniform(-1, 1, size=(300, 96)).astype(np.float32)
-    C, Bu = run_gpu(cuda, A, B, fp32, 16, 64, b_half=not fp32, ldb_pad=8, ldc_pad=12)
+    C, Bu = run_gpu(cuda, A, B, fp32, 16, 64, b_half=not fp32, ldb_pad=8, ldc_pad=12, plan=plan)
     oracle_check(A, C, Bu, fp32)
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
-def test_accumulate_into_c(cuda, fp32):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_accumulate_into_c(cuda, plan, fp32):
     """C += A*B: the reference's contract (its caller zeroes C first, src/main.cpp:242)."""
     rp, col, val = random_csr(128, 256, 0.05, seed=9)
     A = vm.CSR.from_arrays(128, 256, rp, col, val)
     B = np.random.default_rng(9).uniform(-1, 1, size=(256, 128)).astype(np.float32)
     base = np.random.default_rng(10).uniform(-1, 1, size=(128, 128)).astype(np.float32)
-    C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32, accumulate_into=base)
+    C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32, accumulate_into=base, plan=plan)
     oracle_check(A, C, Bu, fp32, base=base.astype(np.float64))
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
-def test_tiny_and_partial_segment(cuda, fp32):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_tiny_and_partial_segment(cuda, plan, fp32):
     """N < segw, M not a multiple of 16, last partial segment zero-filled (src/vcsr_mc.cu:185)."""
     rp, col, val = random_csr(5, 7, 0.6, seed=2)
     A = vm.CSR.from_arrays(5, 7, rp, col, val)
     B = np.random.default_rng(2).uniform(-1, 1, size=(7, 64)).astype(np.float32)
-    C, Bu = run_gpu(cuda, A, B, fp32, 64, 64, b_half=not fp32)
+    C, Bu = run_gpu(cuda, A, B, fp32, 64, 64, b_half=not fp32, plan=plan)
     oracle_check(A, C, Bu, fp32)
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
-def test_empty_matrix(cuda, fp32):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_empty_matrix(cuda, plan, fp32):
     A = vm.CSR.from_arrays(10, 10, np.zeros(11, np.int32), np.zeros(0, np.int32), np.zeros(0, np.float32))
     B = np.ones((10, 32), np.float32)
-    C, _ = run_gpu(cuda, A, B, fp32, 32, 64, b_half=not fp32)
+    C, _ = run_gpu(cuda, A, B, fp32, 32, 64, b_half=not fp32, plan=plan)
     assert np.all(C == 0)
 
 
 @pytest.mark.parametrize("amax", [1e6, 1e-6], ids=["large", "tiny"])
-def test_half_scale_triggers(cuda, amax):
+@pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
+def test_half_scale_triggers(cuda, plan, amax):
     """|A| beyond the fp16 range is scaled by half_scale and C multiplied back (src/vcsr_mc.cu:14-22)."""
     rp, col, val = random_csr(64, 96, 0.1, seed=4, scale=amax)
     A = vm.CSR.from_arrays(64, 96, rp, col, val)
     assert vm.half_scale(A) != 1.0
     B = np.random.default_rng(4).uniform(-1, 1, size=(96, 64)).astype(np.float32)
-    C, Bu = run_gpu(cuda, A, B, False, 32, 64, b_half=True)
+    C, Bu = run_gpu(cuda, A, B, False, 32, 64, b_half=True, plan=plan)
     oracle_check(A, C, Bu, False)
 
 
@@ -197,4 +212,20 @@ def test_errors_are_status_codes(cuda):
     assert e.value.status == 1
     with pytest.raises(vm.VcsrmcError):
         vm.spmm(dV, B.float(), C, tileK=48)
+    dV.free()
+
+
+def test_reference_style_timed_call(cuda):
+    """run_vcsr_mc_spmm_gpu: blocking, event-timed, C += A*B on a caller-zeroed C (src/main.cpp:242-245)."""
+    torch = cuda
+    A = vm.CSR.generate(vm.GEN_UNIFORM_POISSON, 4096, seed=0)
+    B32 = vm.gen_dense_host(4096, 128, seed=0)
+    dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=True, segw=32))
+    B = torch.from_numpy(B32).cuda()
+    C = torch.zeros((4096, 128), device="cuda")
+    ms = vm.run_vcsr_mc_spmm_gpu(dV, B, 128, 128, C)
+    assert ms > 0.0
+    rp, col, val = A.arrays()
+    ref, ab = ob.spmm_fp64(rp, col, val, B32, with_abs=True)
+    check_fp32(C.cpu().numpy(), ref, ab)
     dV.free()

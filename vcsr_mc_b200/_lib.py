@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(_HERE, "libvcsrmc.so")
 OK, INVALID_ARG, CUDA_ERR, OOM, TIMEOUT, IO_ERR, FORMAT_ERR, INTERNAL = range(8)
 F32, F16 = 0, 1
 GEN_UNIFORM_POISSON, GEN_ZIPF, GEN_STENCIL27, GEN_RMAT = 1, 2, 3, 4
+PLAN_AUTO, PLAN_SEGMENT, PLAN_ROWS = 0, 1, 2
 
 _STATUS_NAMES = {
     OK: "OK", INVALID_ARG: "INVALID_ARG", CUDA_ERR: "CUDA_ERR", OOM: "OOM", TIMEOUT: "TIMEOUT",
@@ -75,9 +76,11 @@ PROTOTYPES = {
     "vcsrmc_format_view_get": (_int, [_p, ctypes.POINTER(FormatView)]),
     "vcsrmc_format_free": (None, [_p]),
     "vcsrmc_upload": (_int, [_p, _int, _p, _pp]),
+    "vcsrmc_upload_ex": (_int, [_p, _int, _int, _p, _pp]),
     "vcsrmc_device_free": (_int, [_p]),
     "vcsrmc_device_status": (_int, [_p, ctypes.POINTER(ctypes.c_uint32), _int]),
     "vcsrmc_spmm": (_int, [_p, _p, _int, _i64, _i32, _i32, _p, _i64, _int, _p]),
+    "vcsrmc_spmm_ex": (_int, [_p, _p, _int, _i64, _i32, _i32, _p, _i64, _int, _int, _p]),
     "vcsrmc_spmm_timed": (_int, [_p, _p, _int, _i64, _i32, _i32, _p, _i64, _int, _p, _pf32]),
     "vcsrmc_gen_csr": (_int, [_int, _i32, _u64, _int, _pp]),
     "vcsrmc_gen_dense_host": (_int, [_i64, _i32, _u64, _p, _int]),

@@ -20,7 +20,7 @@ from typing import Optional
 import numpy as np
 
 from . import _lib
-from ._lib import F16, F32, VcsrmcError, call
+from ._lib import F16, F32, PLAN_AUTO, PLAN_ROWS, PLAN_SEGMENT, VcsrmcError, call
 
 
 def _ptr(a: np.ndarray) -> ctypes.c_void_p:
@@ -213,9 +213,12 @@ class DeviceVCSRMC:
         return f.value
 
 
-def upload_vcsr_mc_device(V: VCSRMC, device: int = 0, stream=None) -> DeviceVCSRMC:
+def upload_vcsr_mc_device(V: VCSRMC, device: int = 0, stream=None, plans=None) -> DeviceVCSRMC:
+    """Copies the format to `device`. plans: iterable of PLAN_SEGMENT / PLAN_ROWS layouts to make
+    resident (default: both)."""
+    mask = 0 if plans is None else sum(1 << p for p in set(plans))
     h = ctypes.c_void_p()
-    call("vcsrmc_upload", V.handle, device, _stream_handle(stream), ctypes.byref(h))
+    call("vcsrmc_upload_ex", V.handle, device, mask, _stream_handle(stream), ctypes.byref(h))
     return DeviceVCSRMC(h, V, device)
 
 
@@ -240,12 +243,13 @@ def _check_dense(B, C, O):
         raise VcsrmcError(_lib.INVALID_ARG, "B and C must be 2-D row-major with >= O columns")
 
 
-def spmm(dV: DeviceVCSRMC, B, C, tileK: int = 128, accumulate: bool = False, stream=None, O: Optional[int] = None):
+def spmm(dV: DeviceVCSRMC, B, C, tileK: int = 128, accumulate: bool = False, stream=None, O: Optional[int] = None,
+         plan: int = PLAN_AUTO):
     """C[:, :O] (+)= A * B[:, :O] on the GPU, asynchronous on `stream` (default: torch's current)."""
     O = int(B.shape[1]) if O is None else O
     _check_dense(B, C, O)
-    call("vcsrmc_spmm", dV.handle, ctypes.c_void_p(B.data_ptr()), _b_args(B), B.stride(0), O, tileK,
-         ctypes.c_void_p(C.data_ptr()), C.stride(0), 1 if accumulate else 0, _stream_handle(stream))
+    call("vcsrmc_spmm_ex", dV.handle, ctypes.c_void_p(B.data_ptr()), _b_args(B), B.stride(0), O, tileK,
+         ctypes.c_void_p(C.data_ptr()), C.stride(0), 1 if accumulate else 0, plan, _stream_handle(stream))
     return C
 
 

@@ -10,6 +10,8 @@
 //   val    fp16[n_slots] for the FP16 format (rounded to nearest even, as the reference's
 //          (_Float16) conversion), fp32[n_slots] for the FP32 format
 //   status uint32           kernel error flags (bounded waits)
+// plus, for the ROWS plan (plan_rows.cu), the row view: rp int32[M+1], cols int32[nnz],
+//   vals fp16|fp32[nnz], units int4[n_units], split_rows int32[n_split_rows].
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -21,6 +23,7 @@
 #include "../common/vrng.h"
 #include "../host/parallel.hpp"
 #include "common.cuh"
+#include "plan_rows.hpp"
 #include "spmm_launch.hpp"
 
 struct vcsrmc_device_format {
@@ -34,6 +37,16 @@ struct vcsrmc_device_format {
     int8_t* lcol = nullptr;
     void* val = nullptr;
     uint32_t* status = nullptr;
+    bool has_segment = false;
+    // ROWS plan
+    bool has_rows = false;
+    int4* units = nullptr;
+    int64_t n_units = 0;
+    int* rp = nullptr;
+    int* cols = nullptr;
+    void* rvals = nullptr;
+    int* split_rows = nullptr;
+    int n_split_rows = 0;
 };
 
 namespace vcsrmc {
@@ -83,6 +96,11 @@ void free_device(vcsrmc_device_format* d) {
     cudaFree(d->lcol);
     cudaFree(d->val);
     cudaFree(d->status);
+    cudaFree(d->units);
+    cudaFree(d->rp);
+    cudaFree(d->cols);
+    cudaFree(d->rvals);
+    cudaFree(d->split_rows);
     if (prev >= 0) cudaSetDevice(prev);
     delete d;
 }
@@ -111,6 +129,9 @@ void validate_format(const VCSRMC& v) {
         if (v.group_rows[i] < -1 || v.group_rows[i] >= v.M) bad("group_rows");
     for (int64_t s = 0; s < S; ++s)
         if (v.lcol[s] < -1 || v.lcol[s] >= v.segw) bad("lcol");
+    for (int64_t g = 0; g < G; ++g)
+        for (int64_t s = v.group_ptr[g]; s < v.group_ptr[g + 1]; ++s)
+            if (v.lcol[s] >= 0 && int64_t(v.group_seg_base[g]) + v.lcol[s] >= v.N) bad("column beyond N");
     for (size_t i = 0; i < v.item_gbeg.size(); ++i) {
         const int b = v.item_gbeg[i], e = v.item_gend[i];
         if (b < 0 || e <= b || e > G) bad("item range");
@@ -148,8 +169,37 @@ void check_spmm_args(const vcsrmc_device_format* d, const void* B, int b_dtype, 
     if ((d->N > 0 && !B) || (d->M > 0 && !C)) throw StatusError(VCSRMC_INVALID_ARG, "NULL B or C");
 }
 
+int resolve_plan(const vcsrmc_device_format* d, int plan) {
+    if (plan == VCSRMC_PLAN_AUTO) plan = d->has_rows ? VCSRMC_PLAN_ROWS : VCSRMC_PLAN_SEGMENT;
+    if (plan == VCSRMC_PLAN_ROWS && !d->has_rows)
+        throw StatusError(VCSRMC_INVALID_ARG, "the ROWS plan layout was not uploaded");
+    if (plan == VCSRMC_PLAN_SEGMENT && !d->has_segment)
+        throw StatusError(VCSRMC_INVALID_ARG, "the SEGMENT plan layout was not uploaded");
+    if (plan != VCSRMC_PLAN_ROWS && plan != VCSRMC_PLAN_SEGMENT)
+        throw StatusError(VCSRMC_INVALID_ARG, "unknown plan");
+    return plan;
+}
+
 void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb, int32_t O, int32_t tileK,
-                 float* C, int64_t ldc, int accumulate, cudaStream_t st) {
+                 float* C, int64_t ldc, int accumulate, int plan, cudaStream_t st) {
+    plan = resolve_plan(d, plan);
+    cudaError_t e;
+    if (plan == VCSRMC_PLAN_ROWS) {
+        dev::RowPlanView P;
+        P.units = d->units;
+        P.n_units = d->n_units;
+        P.rp = d->rp;
+        P.cols = d->cols;
+        P.vals = d->rvals;
+        P.vals_f16 = d->fp32 ? 0 : 1;
+        P.split_rows = d->split_rows;
+        P.n_split_rows = d->n_split_rows;
+        P.M = d->M;
+        P.scale = d->scale;
+        e = dev::spmm_rows(P, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, C, ldc, accumulate != 0, st);
+        cuda_check(e, "SpMM launch (rows plan)");
+        return;
+    }
     if (!accumulate && d->M > 0) {
         if (ldc == O)
             cuda_check(cudaMemsetAsync(C, 0, sizeof(float) * size_t(d->M) * size_t(O), st), "cudaMemsetAsync");
@@ -158,12 +208,11 @@ void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int6
                        "cudaMemset2DAsync");
     }
     const dev::DeviceFormatView F = view_of(d);
-    cudaError_t e;
     if (d->fp32)
         e = dev::spmm_fp32_atomic(F, static_cast<const float*>(B), ldb, O, tileK, C, ldc, st);
     else
         e = dev::spmm_fp16_tc_atomic(F, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, tileK, C, ldc, st);
-    cuda_check(e, "SpMM launch");
+    cuda_check(e, "SpMM launch (segment plan)");
 }
 
 __global__ void gen_dense_kernel(int64_t rows, int cols, uint64_t key, int f16, void* out, int64_t ld) {
@@ -197,9 +246,13 @@ cudaError_t gen_dense_device(int64_t rows, int cols, uint64_t seed, int f16, voi
 
 using namespace vcsrmc;
 
-VCSRMC_EXPORT int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out) {
+VCSRMC_EXPORT int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans, void* stream,
+                                   vcsrmc_device_format** out) {
     return guarded([&] {
         if (!f || !out) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        if (plans == 0) plans = (1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS);
+        if (plans & ~((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS)))
+            throw StatusError(VCSRMC_INVALID_ARG, "unknown plan bits");
         const VCSRMC& v = f->v;
         validate_format(v);
         DeviceGuard guard(device);
@@ -217,28 +270,52 @@ VCSRMC_EXPORT int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream
         try {
             const int64_t G = d->n_groups, S = d->n_slots, I = d->n_items;
             const int nth = resolve_threads(0);
-            std::vector<int2> items(I);
-            for (int64_t i = 0; i < I; ++i) items[i] = make_int2(v.item_gbeg[i], v.item_gend[i]);
-            std::vector<int4> gmeta(G);
-            for (int64_t g = 0; g < G; ++g)
-                gmeta[g] = make_int4(v.group_ptr[g], v.group_depth[g], v.group_seg_base[g], 0);
-            std::vector<int8_t> lcol(S);
-            parallel_for(0, S, nth, [&](int64_t a, int64_t b) {
-                for (int64_t s = a; s < b; ++s) lcol[s] = int8_t(v.lcol[s]);
-            });
-            d->items = upload_array(items.data(), items.size(), st);
-            d->gmeta = upload_array(gmeta.data(), gmeta.size(), st);
-            d->grows = upload_array(v.group_rows.data(), v.group_rows.size(), st);
-            d->lcol = upload_array(lcol.data(), lcol.size(), st);
-            if (d->fp32) {
-                d->val = upload_array(v.val.data(), v.val.size(), st);
-            } else {
-                std::vector<__half> h(S);
+            if (plans & (1 << VCSRMC_PLAN_SEGMENT)) {
+                std::vector<int2> items(I);
+                for (int64_t i = 0; i < I; ++i) items[i] = make_int2(v.item_gbeg[i], v.item_gend[i]);
+                std::vector<int4> gmeta(G);
+                for (int64_t g = 0; g < G; ++g)
+                    gmeta[g] = make_int4(v.group_ptr[g], v.group_depth[g], v.group_seg_base[g], 0);
+                std::vector<int8_t> lcol(S);
                 parallel_for(0, S, nth, [&](int64_t a, int64_t b) {
-                    for (int64_t s = a; s < b; ++s) h[s] = __float2half_rn(v.val[s]);
+                    for (int64_t s = a; s < b; ++s) lcol[s] = int8_t(v.lcol[s]);
                 });
-                d->val = upload_array(h.data(), h.size(), st);
+                d->items = upload_array(items.data(), items.size(), st);
+                d->gmeta = upload_array(gmeta.data(), gmeta.size(), st);
+                d->grows = upload_array(v.group_rows.data(), v.group_rows.size(), st);
+                d->lcol = upload_array(lcol.data(), lcol.size(), st);
+                if (d->fp32) {
+                    d->val = upload_array(v.val.data(), v.val.size(), st);
+                } else {
+                    std::vector<__half> h(S);
+                    parallel_for(0, S, nth, [&](int64_t a, int64_t b) {
+                        for (int64_t s = a; s < b; ++s) h[s] = __float2half_rn(v.val[s]);
+                    });
+                    d->val = upload_array(h.data(), h.size(), st);
+                    cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+                }
+                d->has_segment = true;
+            }
+            if (plans & (1 << VCSRMC_PLAN_ROWS)) {
+                dev::RowViewHost rv = dev::build_row_view(v);
+                d->rp = upload_array(rv.rp.data(), rv.rp.size(), st);
+                d->cols = upload_array(rv.cols.data(), rv.cols.size(), st);
+                static_assert(sizeof(dev::RowViewHost::Unit) == sizeof(int4), "unit layout");
+                d->units = reinterpret_cast<int4*>(upload_array(rv.units.data(), rv.units.size(), st));
+                d->n_units = int64_t(rv.units.size());
+                d->split_rows = upload_array(rv.split_rows.data(), rv.split_rows.size(), st);
+                d->n_split_rows = int(rv.split_rows.size());
+                if (d->fp32) {
+                    d->rvals = upload_array(rv.vals.data(), rv.vals.size(), st);
+                } else {
+                    std::vector<__half> h(rv.vals.size());
+                    parallel_for(0, int64_t(h.size()), nth, [&](int64_t a, int64_t b) {
+                        for (int64_t s = a; s < b; ++s) h[s] = __float2half_rn(rv.vals[s]);
+                    });
+                    d->rvals = upload_array(h.data(), h.size(), st);
+                }
                 cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+                d->has_rows = true;
             }
             cuda_check(cudaMalloc(&d->status, sizeof(uint32_t)), "cudaMalloc");
             cuda_check(cudaMemsetAsync(d->status, 0, sizeof(uint32_t), st), "cudaMemsetAsync");
@@ -249,6 +326,10 @@ VCSRMC_EXPORT int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream
         }
         *out = d;
     });
+}
+
+VCSRMC_EXPORT int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out) {
+    return vcsrmc_upload_ex(f, device, 0, stream, out);
 }
 
 VCSRMC_EXPORT int vcsrmc_device_free(vcsrmc_device_format* d) {
@@ -264,13 +345,19 @@ VCSRMC_EXPORT int vcsrmc_device_status(const vcsrmc_device_format* d, uint32_t* 
     });
 }
 
-VCSRMC_EXPORT int vcsrmc_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb, int32_t O,
-                              int32_t tileK, float* C, int64_t ldc, int accumulate, void* stream) {
+VCSRMC_EXPORT int vcsrmc_spmm_ex(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb,
+                                 int32_t O, int32_t tileK, float* C, int64_t ldc, int accumulate, int plan,
+                                 void* stream) {
     return guarded([&] {
         check_spmm_args(d, B, b_dtype, ldb, O, tileK, C, ldc);
         DeviceGuard guard(d->device);
-        launch_spmm(d, B, b_dtype, ldb, O, tileK, C, ldc, accumulate, static_cast<cudaStream_t>(stream));
+        launch_spmm(d, B, b_dtype, ldb, O, tileK, C, ldc, accumulate, plan, static_cast<cudaStream_t>(stream));
     });
+}
+
+VCSRMC_EXPORT int vcsrmc_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb, int32_t O,
+                              int32_t tileK, float* C, int64_t ldc, int accumulate, void* stream) {
+    return vcsrmc_spmm_ex(d, B, b_dtype, ldb, O, tileK, C, ldc, accumulate, VCSRMC_PLAN_AUTO, stream);
 }
 
 VCSRMC_EXPORT int vcsrmc_spmm_timed(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb,
@@ -287,7 +374,7 @@ VCSRMC_EXPORT int vcsrmc_spmm_timed(const vcsrmc_device_format* d, const void* B
         if (e != cudaSuccess) { cudaEventDestroy(t0); cuda_check(e, "cudaEventCreate"); }
         try {
             cuda_check(cudaEventRecord(t0, st), "cudaEventRecord");
-            launch_spmm(d, B, b_dtype, ldb, O, tileK, C, ldc, accumulate, st);
+            launch_spmm(d, B, b_dtype, ldb, O, tileK, C, ldc, accumulate, VCSRMC_PLAN_AUTO, st);
             cuda_check(cudaEventRecord(t1, st), "cudaEventRecord");
             cuda_check(cudaEventSynchronize(t1), "cudaEventSynchronize");
             cuda_check(cudaEventElapsedTime(ms, t0, t1), "cudaEventElapsedTime");

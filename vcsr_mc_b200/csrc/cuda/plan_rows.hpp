@@ -1,0 +1,45 @@
+// Row-stationary SpMM plan over the row view of a VCSR-MC format (see plan_rows.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "vcsrmc/vcsr_formats.hpp"
+
+namespace vcsrmc {
+namespace dev {
+
+constexpr int kUnitNnz = 256;  // entries per warp unit (heavier rows are split into chunks)
+constexpr int kUnitRows = 32;  // light rows per warp unit at most
+
+// Host-side row view: row r's entries are cols/vals[rp[r], rp[r+1]) in ascending column order;
+// units = {first row, end row | 0x80000000 for a heavy-row chunk, first entry, end entry}.
+struct RowViewHost {
+    std::vector<int> rp, cols;
+    std::vector<float> vals;
+    struct Unit { int x, y, z, w; };
+    std::vector<Unit> units;
+    std::vector<int> split_rows;
+};
+
+RowViewHost build_row_view(const VCSRMC& v);
+
+struct RowPlanView {
+    const int4* units;
+    int64_t n_units;
+    const int* rp;
+    const int* cols;
+    const void* vals;  // __half if vals_f16 else float
+    int vals_f16;
+    const int* split_rows;
+    int n_split_rows;
+    int M;
+    float scale;
+};
+
+cudaError_t spmm_rows(const RowPlanView& P, const void* B, int b_is_f16, int64_t ldb, int O, float* C, int64_t ldc,
+                      bool accumulate, cudaStream_t st);
+
+}  // namespace dev
+}  // namespace vcsrmc
