@@ -10,9 +10,12 @@
 //   * a run of up to kUnitRows consecutive light rows with together <= kUnitNnz entries, or
 //   * one kUnitNnz-entry chunk of a heavy row (more than kUnitNnz entries);
 // lane l accumulates columns 4l..4l+3 of a 128-column slab in fp32 registers, gathering the B
-// row of every entry (fp16: one 8-byte load per lane = one 256-byte line per entry) with eight
-// loads in flight per warp; then stores the C row once (16-byte streaming stores), or, for a
-// heavy-row chunk, adds it with one 16-byte vector reduction per lane.
+// row of every entry (fp16: one 8-byte load per lane = one 256-byte line per entry). The warp
+// streams its unit's entries in batches of 32 regardless of row boundaries (the row of each
+// entry comes from a 5-step shuffle search over the unit's row ends), keeps kInFlight gathers
+// in flight, prefetches the next batch's (column, value) pairs, and stores a C row (16-byte
+// streaming stores) when the row changes; a heavy-row chunk instead adds its row with one
+// 16-byte vector reduction per lane.
 // A values and column indices are streamed (evict-first); B keeps the default caching so hot
 // columns stay in L1/L2.
 #include <cuda_fp16.h>
@@ -44,116 +47,172 @@ __device__ __forceinline__ __half ld_stream<__half>(const __half* p) {
     return __ushort_as_half(u);
 }
 
-// Four consecutive B elements (nv of them valid) as fp32.
-template <bool kVec>
-__device__ __forceinline__ float4 load_b4(const __half* p, int nv) {
-    if (kVec && nv == 4) {
-        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
-        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-        return make_float4(lo.x, lo.y, hi.x, hi.y);
+// One lane's share of an entry's B row: 16 bytes = 8 fp16 or 4 fp32 consecutive columns.
+template <typename BT>
+struct Lane16 {
+    static constexpr int kElems = 16 / int(sizeof(BT));  // columns per lane
+    static constexpr int kLanes = 128 / kElems;          // lanes per entry (one 128-column slab)
+};
+
+template <bool kVec, typename BT>
+__device__ __forceinline__ uint4 load16(const BT* p, int nv) {
+    if (kVec && nv == Lane16<BT>::kElems) return __ldg(reinterpret_cast<const uint4*>(p));
+    // ragged tail of O, or unaligned B: element by element, zero beyond O
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if constexpr (sizeof(BT) == 2) {
+        const unsigned short* q = reinterpret_cast<const unsigned short*>(p);
+        for (int i = 0; i < nv; ++i) w[i >> 1] |= uint32_t(q[i]) << ((i & 1) * 16);
+    } else {
+        const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
+        for (int i = 0; i < nv; ++i) w[i] = q[i];
     }
-    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (nv > 0) r.x = __half2float(p[0]);
-    if (nv > 1) r.y = __half2float(p[1]);
-    if (nv > 2) r.z = __half2float(p[2]);
-    if (nv > 3) r.w = __half2float(p[3]);
-    return r;
-}
-template <bool kVec>
-__device__ __forceinline__ float4 load_b4(const float* p, int nv) {
-    if (kVec && nv == 4) return __ldg(reinterpret_cast<const float4*>(p));
-    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (nv > 0) r.x = __ldg(p);
-    if (nv > 1) r.y = __ldg(p + 1);
-    if (nv > 2) r.z = __ldg(p + 2);
-    if (nv > 3) r.w = __ldg(p + 3);
-    return r;
+    return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// acc += A[row, entries p0..p1) * B[:, c0..c0+3]
-template <bool kVec, typename VT, typename BT>
-__device__ __forceinline__ void accumulate_range(float4& acc, int p0, int p1, const int* __restrict__ cols,
-                                                 const VT* __restrict__ vals, const BT* __restrict__ B, int64_t ldb,
-                                                 int c0, int nv, int lane) {
-    constexpr int U = 8;
-    for (int p = p0; p < p1; p += 32) {
-        const int n = min(32, p1 - p);
-        int mc = 0;
-        float mv = 0.f;
-        if (lane < n) {
-            mc = ld_stream(cols + p + lane);
-            mv = to_f(ld_stream(vals + p + lane));
-        }
-        for (int j = 0; j < n; j += U) {
-            float4 b[U];
-            float v[U];
+// acc[i] += a * B_lane[i]
+__device__ __forceinline__ void fma_lane(float (&acc)[8], float a, const uint4& r, __half) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-            for (int k = 0; k < U; ++k) {
-                const int c = __shfl_sync(kFull, mc, (j + k) & 31);
-                v[k] = __shfl_sync(kFull, mv, (j + k) & 31);
-                if (j + k < n) {
-                    b[k] = load_b4<kVec>(B + int64_t(c) * ldb + c0, nv);
-                } else {
-                    b[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    v[k] = 0.f;
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        acc[2 * i] = fmaf(a, f.x, acc[2 * i]);
+        acc[2 * i + 1] = fmaf(a, f.y, acc[2 * i + 1]);
+    }
+}
+__device__ __forceinline__ void fma_lane(float (&acc)[8], float a, const uint4& r, float) {
+    acc[0] = fmaf(a, __uint_as_float(r.x), acc[0]);
+    acc[1] = fmaf(a, __uint_as_float(r.y), acc[1]);
+    acc[2] = fmaf(a, __uint_as_float(r.z), acc[2]);
+    acc[3] = fmaf(a, __uint_as_float(r.w), acc[3]);
+}
+
+// C row segment of this lane: kE columns at dst (nv valid). Overwrite, add, or reduce.
+enum class RowOut { kStore, kAdd, kReduce };
+template <int kE, bool kVec, RowOut kOut>
+__device__ __forceinline__ void write_lane(float* dst, const float (&acc)[8], float scale, int nv) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < kE; ++i) v[i] = acc[i] * scale;
+    if (kVec && nv == kE) {
+#pragma unroll
+        for (int i = 0; i < kE; i += 4) {
+            float4 x = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            float4* d4 = reinterpret_cast<float4*>(dst + i);
+            if constexpr (kOut == RowOut::kReduce) {
+                atomicAdd(d4, x);
+            } else {
+                if constexpr (kOut == RowOut::kAdd) {
+                    const float4 o = *d4;
+                    x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
                 }
+                __stcs(d4, x);
             }
-#pragma unroll
-            for (int k = 0; k < U; ++k) {
-                acc.x = fmaf(v[k], b[k].x, acc.x);
-                acc.y = fmaf(v[k], b[k].y, acc.y);
-                acc.z = fmaf(v[k], b[k].z, acc.z);
-                acc.w = fmaf(v[k], b[k].w, acc.w);
-            }
+        }
+    } else {
+        for (int i = 0; i < nv; ++i) {
+            if constexpr (kOut == RowOut::kReduce) atomicAdd(dst + i, v[i]);
+            else if constexpr (kOut == RowOut::kAdd) dst[i] += v[i];
+            else dst[i] = v[i];
         }
     }
 }
 
+constexpr int kInFlight = 8;  // B gathers in flight per lane group
+
+// A lane group (kLanes lanes: 16 for fp16 B, 32 for fp32 B) owns one work unit and one 128-column
+// slab of C; lane l of the group holds columns c0 .. c0+kE-1 of it.
 template <bool kVec, bool kAccumulate, typename VT, typename BT>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     vcsr_rows_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
                      const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
                      int64_t ldb, int O, float* __restrict__ C, int64_t ldc, float scale) {
+    constexpr int kE = Lane16<BT>::kElems;
+    constexpr int kL = Lane16<BT>::kLanes;
+    constexpr int kGroups = 32 / kL;
     const int lane = threadIdx.x & 31;
-    const int64_t w = int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
-    if (w >= n_units) return;
-    const int4 u = units[w];
-    const int c0 = blockIdx.y * 128 + 4 * lane;
-    const int nv = max(0, min(4, O - c0));
+    const int sub = lane / kL, sl = lane % kL;
+    const unsigned gmask = kL == 32 ? kFull : (0xffffu << (16 * sub));
+    const int64_t unit = (int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5)) * kGroups + sub;
+    if (unit >= n_units) return;  // the whole group leaves together
+    const int4 u = units[unit];
+    const int c0 = blockIdx.y * 128 + kE * sl;
+    const int nv = max(0, min(kE, O - c0));
     const bool partial = (u.y & 0x80000000) != 0;
-    const int r_end = u.y & 0x7fffffff;
-    if (partial) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        accumulate_range<kVec>(acc, u.z, u.w, cols, vals, B, ldb, c0, nv, lane);
-        float* dst = C + int64_t(u.x) * ldc + c0;
-        acc.x *= scale; acc.y *= scale; acc.z *= scale; acc.w *= scale;
-        if (kVec && nv == 4) {
-            atomicAdd(reinterpret_cast<float4*>(dst), acc);
-        } else {
-            if (nv > 0) atomicAdd(dst, acc.x);
-            if (nv > 1) atomicAdd(dst + 1, acc.y);
-            if (nv > 2) atomicAdd(dst + 2, acc.z);
-            if (nv > 3) atomicAdd(dst + 3, acc.w);
+    const int rb = u.x, pb = u.z, pe = u.w;
+    const int nrows = partial ? 1 : (u.y & 0x7fffffff) - rb;
+
+    // Row ends of the unit's rows (<= kUnitRows <= kL), one per lane.
+    const int my_end = (!partial && sl < nrows) ? rp[rb + sl + 1] : 0x7fffffff;
+    if (!partial && !kAccumulate) {
+        // rows without entries are written here; the others when their last entry is done
+        // every lane of the group takes part in the shuffle (lane 0's result is replaced)
+        const int prev_end = __shfl_up_sync(gmask, my_end, 1, kL);
+        const int my_start = sl == 0 ? pb : prev_end;
+        unsigned empty = __ballot_sync(gmask, sl < nrows && my_start == my_end);
+        if (kL == 16) empty = (empty >> (16 * sub)) & 0xffffu;
+        const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        while (empty) {
+            const int i = __ffs(empty) - 1;
+            empty &= empty - 1;
+            write_lane<kE, kVec, RowOut::kStore>(C + int64_t(rb + i) * ldc + c0, zero, 1.f, nv);
         }
-        return;
     }
-    for (int r = u.x; r < r_end; ++r) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        accumulate_range<kVec>(acc, rp[r], rp[r + 1], cols, vals, B, ldb, c0, nv, lane);
-        acc.x *= scale; acc.y *= scale; acc.z *= scale; acc.w *= scale;
-        float* dst = C + int64_t(r) * ldc + c0;
-        if (kVec && nv == 4) {
-            if (kAccumulate) {
-                const float4 old = *reinterpret_cast<const float4*>(dst);
-                acc.x += old.x; acc.y += old.y; acc.z += old.z; acc.w += old.w;
+
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // software pipeline: the next batch's (column, value) are loaded while this batch gathers B
+    int mc = 0;
+    float mv = 0.f;
+    if (pb + sl < pe) {
+        mc = ld_stream(cols + pb + sl);
+        mv = to_f(ld_stream(vals + pb + sl));
+    }
+    for (int q = pb; q < pe; q += kL) {
+        const int n = min(kL, pe - q);
+        const int cmc = mc;
+        const float cmv = mv;
+        if (q + kL + sl < pe) {
+            mc = ld_stream(cols + q + kL + sl);
+            mv = to_f(ld_stream(vals + q + kL + sl));
+        }
+        // local row of this lane's entry (number of unit rows that end at or before it), and
+        // whether the entry is the last of its row
+        int lo = 0;
+        unsigned ends = 0;
+        if (!partial) {
+            const int e = q + sl;
+#pragma unroll
+            for (int step = kUnitRows / 2; step >= 1; step >>= 1) {
+                const int probe = __shfl_sync(gmask, my_end, (lo + step - 1) & (kL - 1), kL);
+                if (probe <= e) lo += step;
             }
-            __stcs(reinterpret_cast<float4*>(dst), acc);
-        } else {
-            const float a[4] = {acc.x, acc.y, acc.z, acc.w};
-            for (int i = 0; i < nv; ++i) dst[i] = kAccumulate ? dst[i] + a[i] : a[i];
+            const int row_end = __shfl_sync(gmask, my_end, lo & (kL - 1), kL);
+            ends = __ballot_sync(gmask, sl < n && e + 1 == row_end);
+            if (kL == 16) ends = (ends >> (16 * sub)) & 0xffffu;
+        }
+        for (int j = 0; j < n; j += kInFlight) {
+            uint4 raw[kInFlight];
+#pragma unroll
+            for (int k = 0; k < kInFlight; ++k) {
+                const int c = __shfl_sync(gmask, cmc, (j + k) & (kL - 1), kL);
+                if (j + k < n) raw[k] = load16<kVec>(B + int64_t(c) * ldb + c0, nv);
+            }
+#pragma unroll
+            for (int k = 0; k < kInFlight; ++k) {
+                const float a = __shfl_sync(gmask, cmv, (j + k) & (kL - 1), kL);
+                if (j + k < n) {
+                    fma_lane(acc, a, raw[k], BT());
+                    if ((ends >> (j + k)) & 1u) {
+                        const int row = rb + __shfl_sync(gmask, lo, (j + k) & (kL - 1), kL);
+                        write_lane<kE, kVec, kAccumulate ? RowOut::kAdd : RowOut::kStore>(
+                            C + int64_t(row) * ldc + c0, acc, scale, nv);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+                    }
+                }
+            }
         }
     }
+    if (partial) write_lane<kE, kVec, RowOut::kReduce>(C + int64_t(rb) * ldc + c0, acc, scale, nv);
 }
 
 // Zeroes C's heavy rows (the ones built from several reduced chunks) before an overwrite.
@@ -167,7 +226,9 @@ __global__ void zero_rows_kernel(const int* __restrict__ rows, int n_rows, int O
 template <bool kVec, bool kAcc, typename VT, typename BT>
 cudaError_t launch_rows_t(const RowPlanView& P, const BT* B, int64_t ldb, int O, float* C, int64_t ldc,
                           cudaStream_t st) {
-    const int64_t blocks = (P.n_units + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    constexpr int kGroupsPerWarp = 32 / Lane16<BT>::kLanes;
+    const int64_t per_block = int64_t(kWarpsPerBlock) * kGroupsPerWarp;
+    const int64_t blocks = (P.n_units + per_block - 1) / per_block;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
     const dim3 grid(unsigned(blocks), unsigned((O + 127) / 128));
     vcsr_rows_kernel<kVec, kAcc, VT, BT><<<grid, kWarpsPerBlock * 32, 0, st>>>(
@@ -178,8 +239,9 @@ cudaError_t launch_rows_t(const RowPlanView& P, const BT* B, int64_t ldb, int O,
 template <typename VT, typename BT>
 cudaError_t launch_rows_b(const RowPlanView& P, const BT* B, int64_t ldb, int O, float* C, int64_t ldc,
                           bool accumulate, cudaStream_t st) {
-    const bool vec = (ldb % 4 == 0) && (ldc % 4 == 0) && (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
-                     (reinterpret_cast<uintptr_t>(C) % 16 == 0);
+    // 16-byte B loads and C stores need 16-byte aligned rows
+    const bool vec = ((ldb * int64_t(sizeof(BT))) % 16 == 0) && (ldc % 4 == 0) &&
+                     (reinterpret_cast<uintptr_t>(B) % 16 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0);
     if (vec) {
         return accumulate ? launch_rows_t<true, true, VT, BT>(P, B, ldb, O, C, ldc, st)
                           : launch_rows_t<true, false, VT, BT>(P, B, ldb, O, C, ldc, st);

@@ -11,7 +11,7 @@ namespace vcsrmc {
 namespace dev {
 
 constexpr int kUnitNnz = 256;  // entries per warp unit (heavier rows are split into chunks)
-constexpr int kUnitRows = 32;  // light rows per warp unit at most
+constexpr int kUnitRows = 16;  // light rows per unit at most (one row end per lane of a 16-lane group)
 
 // Host-side row view: row r's entries are cols/vals[rp[r], rp[r+1]) in ascending column order;
 // units = {first row, end row | 0x80000000 for a heavy-row chunk, first entry, end entry}.
