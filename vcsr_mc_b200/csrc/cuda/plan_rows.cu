@@ -6,16 +6,15 @@
 // read-modify-writes per group: for the 2^24-row R-MAT about 127 GB of reductions for a
 // 12 GB job. This plan consumes the same VCSR-MC data transposed at upload time into a row
 // view: row r's entries are its (group, lane) slots over all groups in format order, i.e. in
-// ascending segment and local column. One warp owns a unit of work:
+// ascending segment and local column. A lane group owns a unit of work:
 //   * a run of up to kUnitRows consecutive light rows with together <= kUnitNnz entries, or
 //   * one kUnitNnz-entry chunk of a heavy row (more than kUnitNnz entries);
-// lane l accumulates columns 4l..4l+3 of a 128-column slab in fp32 registers, gathering the B
-// row of every entry (fp16: one 8-byte load per lane = one 256-byte line per entry). The warp
-// streams its unit's entries in batches of 32 regardless of row boundaries (the row of each
-// entry comes from a 5-step shuffle search over the unit's row ends), keeps kInFlight gathers
-// in flight, prefetches the next batch's (column, value) pairs, and stores a C row (16-byte
-// streaming stores) when the row changes; a heavy-row chunk instead adds its row with one
-// 16-byte vector reduction per lane.
+// each lane gathers 16 bytes of every entry's B row (fp16 B: 16 lanes cover one 256-byte row,
+// so a warp runs two units; fp32 B: 32 lanes), accumulates in fp32 registers, and stores a C
+// row once, at its last entry (16-byte streaming stores); a heavy-row chunk adds its partial
+// row with 16-byte vector reductions instead. The group streams the unit's entries in batches
+// regardless of row boundaries: the row of each entry comes from a 4-step shuffle search over
+// the unit's row ends and a ballot marks the last entry of every row.
 // A values and column indices are streamed (evict-first); B keeps the default caching so hot
 // columns stay in L1/L2.
 #include <cuda_fp16.h>
@@ -33,19 +32,6 @@ namespace {
 
 constexpr int kWarpsPerBlock = 8;
 constexpr unsigned kFull = 0xffffffffu;
-
-__device__ __forceinline__ float to_f(float v) { return v; }
-__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
-
-template <typename T>
-__device__ __forceinline__ T ld_stream(const T* p) {
-    return __ldcs(p);
-}
-template <>
-__device__ __forceinline__ __half ld_stream<__half>(const __half* p) {
-    const unsigned short u = __ldcs(reinterpret_cast<const unsigned short*>(p));
-    return __ushort_as_half(u);
-}
 
 // One lane's share of an entry's B row: 16 bytes = 8 fp16 or 4 fp32 consecutive columns.
 template <typename BT>
@@ -69,21 +55,52 @@ __device__ __forceinline__ uint4 load16(const BT* p, int nv) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// acc[i] += a * B_lane[i]
-__device__ __forceinline__ void fma_lane(float (&acc)[8], float a, const uint4& r, __half) {
-    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+// acc[i] += a * B_lane[i]. fp16 x fp16 uses the mixed-precision FMA (f16 inputs, f32 accumulate:
+// the product of two f16 values is exact in f32, so this equals converting first and FFMA).
+__device__ __forceinline__ void fma2_f16(float& d0, float& d1, unsigned short a, uint32_t b2) {
+    asm("{\n\t.reg .b16 blo, bhi;\n\t"
+        "mov.b32 {blo, bhi}, %3;\n\t"
+        "fma.rn.f32.f16 %0, %2, blo, %0;\n\t"
+        "fma.rn.f32.f16 %1, %2, bhi, %1;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "h"(a), "r"(b2));
+}
+// a holds the A value: fp16 bits in the low half (fp16 x fp16) or fp32 bits (otherwise)
+template <typename VT, typename BT>
+__device__ __forceinline__ void fma_lane(float (&acc)[8], uint32_t a, const uint4& r) {
+    if constexpr (sizeof(BT) == 2) {
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+        if constexpr (sizeof(VT) == 2) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        acc[2 * i] = fmaf(a, f.x, acc[2 * i]);
-        acc[2 * i + 1] = fmaf(a, f.y, acc[2 * i + 1]);
+            for (int i = 0; i < 4; ++i) fma2_f16(acc[2 * i], acc[2 * i + 1], (unsigned short)(a & 0xffffu), w[i]);
+        } else {
+            const float af = __uint_as_float(a);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                acc[2 * i] = fmaf(af, f.x, acc[2 * i]);
+                acc[2 * i + 1] = fmaf(af, f.y, acc[2 * i + 1]);
+            }
+        }
+    } else {
+        const float af = __uint_as_float(a);
+        acc[0] = fmaf(af, __uint_as_float(r.x), acc[0]);
+        acc[1] = fmaf(af, __uint_as_float(r.y), acc[1]);
+        acc[2] = fmaf(af, __uint_as_float(r.z), acc[2]);
+        acc[3] = fmaf(af, __uint_as_float(r.w), acc[3]);
     }
 }
-__device__ __forceinline__ void fma_lane(float (&acc)[8], float a, const uint4& r, float) {
-    acc[0] = fmaf(a, __uint_as_float(r.x), acc[0]);
-    acc[1] = fmaf(a, __uint_as_float(r.y), acc[1]);
-    acc[2] = fmaf(a, __uint_as_float(r.z), acc[2]);
-    acc[3] = fmaf(a, __uint_as_float(r.w), acc[3]);
+
+// The A value of an entry as the bits fma_lane expects.
+template <typename VT, typename BT>
+__device__ __forceinline__ uint32_t a_bits(const VT* p) {
+    if constexpr (sizeof(VT) == 2) {
+        const unsigned short h = __ldcs(reinterpret_cast<const unsigned short*>(p));
+        if constexpr (sizeof(BT) == 2) return h;
+        return __float_as_uint(__half2float(__ushort_as_half(h)));
+    } else {
+        return __float_as_uint(__ldcs(p));
+    }
 }
 
 // C row segment of this lane: kE columns at dst (nv valid). Overwrite, add, or reduce.
@@ -117,26 +134,34 @@ __device__ __forceinline__ void write_lane(float* dst, const float (&acc)[8], fl
     }
 }
 
-constexpr int kInFlight = 8;  // B gathers in flight per lane group
+constexpr int kInFlight = 8;  // B gathers in flight per lane
 
-// A lane group (kLanes lanes: 16 for fp16 B, 32 for fp32 B) owns one work unit and one 128-column
-// slab of C; lane l of the group holds columns c0 .. c0+kE-1 of it.
+// A lane group (kL lanes: 16 for fp16 B, 32 for fp32 B) owns one work unit and one 128-column
+// slab of C; lane sl of the group holds columns c0 .. c0+kE-1 of it. Per batch of kL entries the
+// group stages (column, A value) in shared memory (one 8-byte broadcast read per entry later),
+// pads the batch past the unit's end with (column 0, value 0) so no bounds tests are needed,
+// and gathers B eight entries at a time; runs of eight entries without a row end skip the
+// per-entry row-end test.
 template <bool kVec, bool kAccumulate, typename VT, typename BT>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     vcsr_rows_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
                      const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
-                     int64_t ldb, int O, float* __restrict__ C, int64_t ldc, float scale) {
+                     int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale) {
     constexpr int kE = Lane16<BT>::kElems;
     constexpr int kL = Lane16<BT>::kLanes;
     constexpr int kGroups = 32 / kL;
+    constexpr RowOut kOut = kAccumulate ? RowOut::kAdd : RowOut::kStore;
+    __shared__ int2 stage_all[kWarpsPerBlock * 32];
     const int lane = threadIdx.x & 31;
     const int sub = lane / kL, sl = lane % kL;
     const unsigned gmask = kL == 32 ? kFull : (0xffffu << (16 * sub));
+    int2* stage = stage_all + (threadIdx.x >> 5) * 32 + sub * kL;
     const int64_t unit = (int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5)) * kGroups + sub;
     if (unit >= n_units) return;  // the whole group leaves together
     const int4 u = units[unit];
     const int c0 = blockIdx.y * 128 + kE * sl;
     const int nv = max(0, min(kE, O - c0));
+    const char* bbase = reinterpret_cast<const char*>(B) + size_t(c0) * sizeof(BT);
     const bool partial = (u.y & 0x80000000) != 0;
     const int rb = u.x, pb = u.z, pe = u.w;
     const int nrows = partial ? 1 : (u.y & 0x7fffffff) - rb;
@@ -145,7 +170,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     const int my_end = (!partial && sl < nrows) ? rp[rb + sl + 1] : 0x7fffffff;
     if (!partial && !kAccumulate) {
         // rows without entries are written here; the others when their last entry is done
-        // every lane of the group takes part in the shuffle (lane 0's result is replaced)
+        // (every lane of the group takes part in the shuffle; lane 0's result is replaced)
         const int prev_end = __shfl_up_sync(gmask, my_end, 1, kL);
         const int my_start = sl == 0 ? pb : prev_end;
         unsigned empty = __ballot_sync(gmask, sl < nrows && my_start == my_end);
@@ -159,20 +184,21 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     }
 
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    // software pipeline: the next batch's (column, value) are loaded while this batch gathers B
+    // (column, A value) of the lane's entry in the next batch; (0, 0) past the unit's end
     int mc = 0;
-    float mv = 0.f;
+    uint32_t mv = 0;
     if (pb + sl < pe) {
-        mc = ld_stream(cols + pb + sl);
-        mv = to_f(ld_stream(vals + pb + sl));
+        mc = __ldcs(cols + pb + sl);
+        mv = a_bits<VT, BT>(vals + pb + sl);
     }
     for (int q = pb; q < pe; q += kL) {
         const int n = min(kL, pe - q);
-        const int cmc = mc;
-        const float cmv = mv;
+        stage[sl] = make_int2(mc, int(mv));
+        mc = 0;
+        mv = 0;
         if (q + kL + sl < pe) {
-            mc = ld_stream(cols + q + kL + sl);
-            mv = to_f(ld_stream(vals + q + kL + sl));
+            mc = __ldcs(cols + q + kL + sl);
+            mv = a_bits<VT, BT>(vals + q + kL + sl);
         }
         // local row of this lane's entry (number of unit rows that end at or before it), and
         // whether the entry is the last of its row
@@ -189,28 +215,34 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
             ends = __ballot_sync(gmask, sl < n && e + 1 == row_end);
             if (kL == 16) ends = (ends >> (16 * sub)) & 0xffffu;
         }
+        __syncwarp(gmask);
         for (int j = 0; j < n; j += kInFlight) {
             uint4 raw[kInFlight];
+            uint32_t av[kInFlight];
 #pragma unroll
             for (int k = 0; k < kInFlight; ++k) {
-                const int c = __shfl_sync(gmask, cmc, (j + k) & (kL - 1), kL);
-                if (j + k < n) raw[k] = load16<kVec>(B + int64_t(c) * ldb + c0, nv);
+                const int2 e = stage[j + k];
+                av[k] = uint32_t(e.y);
+                raw[k] = load16<kVec>(reinterpret_cast<const BT*>(bbase + int64_t(e.x) * row_bytes), nv);
             }
+            const unsigned eb = (ends >> j) & ((1u << kInFlight) - 1u);
+            if (eb == 0) {
 #pragma unroll
-            for (int k = 0; k < kInFlight; ++k) {
-                const float a = __shfl_sync(gmask, cmv, (j + k) & (kL - 1), kL);
-                if (j + k < n) {
-                    fma_lane(acc, a, raw[k], BT());
-                    if ((ends >> (j + k)) & 1u) {
-                        const int row = rb + __shfl_sync(gmask, lo, (j + k) & (kL - 1), kL);
-                        write_lane<kE, kVec, kAccumulate ? RowOut::kAdd : RowOut::kStore>(
-                            C + int64_t(row) * ldc + c0, acc, scale, nv);
+                for (int k = 0; k < kInFlight; ++k) fma_lane<VT, BT>(acc, av[k], raw[k]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < kInFlight; ++k) {
+                    fma_lane<VT, BT>(acc, av[k], raw[k]);
+                    if ((eb >> k) & 1u) {
+                        const int row = rb + __shfl_sync(gmask, lo, j + k, kL);
+                        write_lane<kE, kVec, kOut>(C + int64_t(row) * ldc + c0, acc, scale, nv);
 #pragma unroll
                         for (int i = 0; i < 8; ++i) acc[i] = 0.f;
                     }
                 }
             }
         }
+        __syncwarp(gmask);
     }
     if (partial) write_lane<kE, kVec, RowOut::kReduce>(C + int64_t(rb) * ldc + c0, acc, scale, nv);
 }
@@ -232,13 +264,15 @@ cudaError_t launch_rows_t(const RowPlanView& P, const BT* B, int64_t ldb, int O,
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
     const dim3 grid(unsigned(blocks), unsigned((O + 127) / 128));
     vcsr_rows_kernel<kVec, kAcc, VT, BT><<<grid, kWarpsPerBlock * 32, 0, st>>>(
-        P.units, P.n_units, P.rp, P.cols, static_cast<const VT*>(P.vals), B, ldb, O, C, ldc, P.scale);
+        P.units, P.n_units, P.rp, P.cols, static_cast<const VT*>(P.vals), B, int(ldb * int64_t(sizeof(BT))), O, C, ldc,
+        P.scale);
     return cudaGetLastError();
 }
 
 template <typename VT, typename BT>
 cudaError_t launch_rows_b(const RowPlanView& P, const BT* B, int64_t ldb, int O, float* C, int64_t ldc,
                           bool accumulate, cudaStream_t st) {
+    if (ldb * int64_t(sizeof(BT)) > 0x7fffffffLL) return cudaErrorInvalidValue;  // row pitch must fit 31 bits
     // 16-byte B loads and C stores need 16-byte aligned rows
     const bool vec = ((ldb * int64_t(sizeof(BT))) % 16 == 0) && (ldc % 4 == 0) &&
                      (reinterpret_cast<uintptr_t>(B) % 16 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0);
