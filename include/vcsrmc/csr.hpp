@@ -7,10 +7,20 @@
 // turns them into status codes.
 #pragma once
 #include <cstdint>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
 namespace vcsrmc {
+
+// Thrown for a file that cannot be opened / for malformed or unsupported matrix data. Both
+// derive from std::runtime_error, as the reference's errors do.
+struct IoError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+struct FormatError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
 
 struct COO {
     int M{0}, N{0};

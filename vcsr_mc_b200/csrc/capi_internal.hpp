@@ -41,14 +41,12 @@ int guarded(Fn&& fn) {
         return fail(e.status, e.what());
     } catch (const std::bad_alloc&) {
         return fail(VCSRMC_OOM, "host allocation failed");
+    } catch (const IoError& e) {
+        return fail(VCSRMC_IO_ERR, e.what());
+    } catch (const FormatError& e) {
+        return fail(VCSRMC_FORMAT_ERR, e.what());
     } catch (const std::exception& e) {
-        const std::string m = e.what();
-        int s = VCSRMC_INVALID_ARG;
-        if (m.rfind("Failed to open MTX", 0) == 0) s = VCSRMC_IO_ERR;
-        else if (m.find("MTX") != std::string::npos || m.find("Duplicate") != std::string::npos ||
-                 m.find("idx out of range") != std::string::npos)
-            s = VCSRMC_FORMAT_ERR;
-        return fail(s, m);
+        return fail(VCSRMC_INVALID_ARG, e.what());
     } catch (...) {
         return fail(VCSRMC_INTERNAL, "unknown exception");
     }

@@ -90,28 +90,28 @@ bool next_data_line(std::ifstream& in, std::string& line) {
 
 COO read_matrix_market_coo(const std::string& path) {
     std::ifstream in(path);
-    if (!in) throw std::runtime_error("Failed to open MTX: " + path);
+    if (!in) throw IoError("Failed to open MTX: " + path);
     std::string line;
-    if (!std::getline(in, line)) throw std::runtime_error("Empty MTX file");
+    if (!std::getline(in, line)) throw FormatError("Empty MTX file");
     LineScanner banner(line);
     const std::string magic = banner.word(), object = banner.word(), layout = banner.word();
     const std::string field = banner.word(), symmetry = banner.word();
     if (magic != "%%MatrixMarket" || object != "matrix" || layout != "coordinate")
-        throw std::runtime_error("Expected a Matrix Market coordinate matrix");
+        throw FormatError("Expected a Matrix Market coordinate matrix");
     if (field != "real" && field != "integer" && field != "pattern")
-        throw std::runtime_error("Unsupported MTX field: " + field);
+        throw FormatError("Unsupported MTX field: " + field);
     if (symmetry != "general" && symmetry != "symmetric" && symmetry != "skew-symmetric")
-        throw std::runtime_error("Unsupported MTX symmetry: " + symmetry);
+        throw FormatError("Unsupported MTX symmetry: " + symmetry);
 
-    if (!next_data_line(in, line)) throw std::runtime_error("Missing MTX dimensions");
+    if (!next_data_line(in, line)) throw FormatError("Missing MTX dimensions");
     long long m = 0, n = 0, count = 0;
     {
         LineScanner dims(line);
         if (!dims.integer(m) || !dims.integer(n) || !dims.integer(count) || m <= 0 || n <= 0 ||
             m >= INT_MAX || n >= INT_MAX || count < 0 || count > INT_MAX)
-            throw std::runtime_error("Invalid or unsupported MTX dimensions/nnz");
+            throw FormatError("Invalid or unsupported MTX dimensions/nnz");
     }
-    if (symmetry != "general" && m != n) throw std::runtime_error("Symmetric MTX must be square");
+    if (symmetry != "general" && m != n) throw FormatError("Symmetric MTX must be square");
 
     const bool pattern = field == "pattern";
     const bool general = symmetry == "general";
@@ -125,29 +125,29 @@ COO read_matrix_market_coo(const std::string& path) {
     coo.vals.reserve(coo.rows.capacity());
     auto append = [&](int r, int c, float v) {
         if (coo.vals.size() >= size_t(INT_MAX))
-            throw std::runtime_error("Expanded MTX exceeds 32-bit nnz limit");
+            throw FormatError("Expanded MTX exceeds 32-bit nnz limit");
         coo.rows.push_back(r);
         coo.cols.push_back(c);
         coo.vals.push_back(v);
     };
     for (long long i = 0; i < count; ++i) {
-        if (!next_data_line(in, line)) throw std::runtime_error("Truncated MTX data");
+        if (!next_data_line(in, line)) throw FormatError("Truncated MTX data");
         LineScanner e(line);
         long long r = 0, c = 0;
         double value = 1.0;
         if (!e.integer(r) || !e.integer(c) || (!pattern && !e.real(value)))
-            throw std::runtime_error("Bad MTX entry at index " + std::to_string(i));
-        if (!e.at_end()) throw std::runtime_error("Extra fields in MTX entry");
+            throw FormatError("Bad MTX entry at index " + std::to_string(i));
+        if (!e.at_end()) throw FormatError("Extra fields in MTX entry");
         if (r < 1 || r > m || c < 1 || c > n)
-            throw std::runtime_error("MTX row/column index out of range (expected one-based indices)");
+            throw FormatError("MTX row/column index out of range (expected one-based indices)");
         if (!std::isfinite(value) || std::abs(value) > std::numeric_limits<float>::max())
-            throw std::runtime_error("MTX value is not finite FP32");
+            throw FormatError("MTX value is not finite FP32");
         if (skew && r == c && value != 0)
-            throw std::runtime_error("Skew-symmetric MTX diagonal must be zero");
+            throw FormatError("Skew-symmetric MTX diagonal must be zero");
         append(int(r - 1), int(c - 1), float(value));
         if (!general && r != c) append(int(c - 1), int(r - 1), float(skew ? -value : value));
     }
-    if (next_data_line(in, line)) throw std::runtime_error("Extra entries after declared MTX nnz");
+    if (next_data_line(in, line)) throw FormatError("Extra entries after declared MTX nnz");
     return coo;
 }
 
@@ -160,7 +160,7 @@ CSR coo_to_csr(const COO& coo) {
     csr.col.resize(csr.nnz);
     csr.val.resize(csr.nnz);
     for (int r : coo.rows) {
-        if (r < 0 || r >= csr.M) throw std::runtime_error("row idx out of range");
+        if (r < 0 || r >= csr.M) throw FormatError("row idx out of range");
         csr.row_ptr[size_t(r) + 1]++;
     }
     for (int i = 1; i <= csr.M; ++i) csr.row_ptr[i] += csr.row_ptr[i - 1];
@@ -168,7 +168,7 @@ CSR coo_to_csr(const COO& coo) {
     for (size_t i = 0; i < coo.vals.size(); ++i) {
         const int dst = cursor[coo.rows[i]]++;
         if (coo.cols[i] < 0 || coo.cols[i] >= csr.N)
-            throw std::runtime_error("column idx out of range");
+            throw FormatError("column idx out of range");
         csr.col[dst] = coo.cols[i];
         csr.val[dst] = coo.vals[i];
     }
@@ -188,7 +188,7 @@ CSR coo_to_csr(const COO& coo) {
         }
         for (int i = s + 1; i < e; ++i)
             if (csr.col[i] == csr.col[i - 1])
-                throw std::runtime_error(
+                throw FormatError(
                     "Duplicate MTX coordinates are unsupported; coalesce them before benchmarking");
     }
     return csr;
