@@ -119,12 +119,16 @@ int vcsrmc_half_scale(const vcsrmc_csr* csr, float* scale);
 int vcsrmc_build_host(const vcsrmc_csr* csr, int fp32, int segw, int nthreads,
                       vcsrmc_format** out);
 int vcsrmc_format_view_get(const vcsrmc_format* f, vcsrmc_format_view* out);
+/* Copies a format given as arrays (e.g. one built by another implementation of
+ * csr_to_vcsr_mc) into a library handle; vcsrmc_upload validates its indices. */
+int vcsrmc_format_from_view(const vcsrmc_format_view* v, vcsrmc_format** out);
 void vcsrmc_format_free(vcsrmc_format* f);
 
 /* ---- device format: src/vcsr_mc.cu:332-349 upload_vcsr_mc_device, :397-404
  *      destroy_vcsr_mc_device ------------------------------------------------------------ */
-/* Validates the format's index arrays on the host, then copies them to `device` in the
- * kernels' layout (FP16 formats keep fp16 values on the device). Blocking. */
+/* Validates the format's index arrays on the host, then copies them to `device` (< 0: the
+ * calling thread's current device) in the kernels' layout (FP16 formats keep fp16 values on
+ * the device). Blocking. */
 int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out);
 /* Same, choosing which plan layouts to make resident: a bit mask of (1 << VCSRMC_PLAN_SEGMENT)
  * and (1 << VCSRMC_PLAN_ROWS); 0 = all (what vcsrmc_upload does). */

@@ -11,6 +11,10 @@
 #include <string>
 #include <vector>
 
+#ifndef VCSRMC_CXX_API
+#define VCSRMC_CXX_API __attribute__((visibility("default")))
+#endif
+
 namespace vcsrmc {
 
 // Thrown for a file that cannot be opened / for malformed or unsupported matrix data. Both
@@ -38,13 +42,13 @@ struct CSR {
 // Parses a Matrix Market "coordinate" file (real | integer | pattern; general | symmetric |
 // skew-symmetric). Indices are one-based in the file; symmetric entries are expanded; values
 // must be finite fp32; the expanded entry count must fit a signed 32-bit int.
-COO read_matrix_market_coo(const std::string& path);
+VCSRMC_CXX_API COO read_matrix_market_coo(const std::string& path);
 
 // Counting sort by row, then ascending columns within each row. Throws on an index out of
 // range and on a duplicate (row, column) coordinate.
-CSR coo_to_csr(const COO& coo);
+VCSRMC_CXX_API CSR coo_to_csr(const COO& coo);
 
 // Rows [r0, r1) of `csr` as a CSR of their own (row ids rebased to 0; columns unchanged).
-CSR csr_row_slice(const CSR& csr, int r0, int r1);
+VCSRMC_CXX_API CSR csr_row_slice(const CSR& csr, int r0, int r1);
 
 }  // namespace vcsrmc

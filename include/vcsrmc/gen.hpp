@@ -7,31 +7,35 @@
 #include <vector>
 #include "csr.hpp"
 
+#ifndef VCSRMC_CXX_API
+#define VCSRMC_CXX_API __attribute__((visibility("default")))
+#endif
+
 namespace vcsrmc {
 
 // M x N, row length ~ Poisson(lambda) (inverse CDF), columns uniform without replacement
 // (Floyd's algorithm), values U(-1,1).
-CSR gen_uniform_poisson(int M, int N, double lambda, uint64_t seed, int nthreads = 0);
+VCSRMC_CXX_API CSR gen_uniform_poisson(int M, int N, double lambda, uint64_t seed, int nthreads = 0);
 
 // M x N, row length k ~ Zipf(s) truncated to [1, kmax] (inverse CDF), then
 // clamp(round(k * mean / E[k]), 1, kmax); columns uniform without replacement; values U(-1,1).
-CSR gen_zipf_rows(int M, int N, double s, int kmax, double mean, uint64_t seed, int nthreads = 0);
-double zipf_length_factor(double s, int kmax, double mean);
+VCSRMC_CXX_API CSR gen_zipf_rows(int M, int N, double s, int kmax, double mean, uint64_t seed, int nthreads = 0);
+VCSRMC_CXX_API double zipf_length_factor(double s, int kmax, double mean);
 
 // 27-point stencil on an nx x ny x nz grid in natural (x fastest) order; diagonal 26,
 // off-diagonal -1 + U(-0.01, 0.01).
-CSR gen_stencil27(int nx, int ny, int nz, uint64_t seed, int nthreads = 0);
+VCSRMC_CXX_API CSR gen_stencil27(int nx, int ny, int nz, uint64_t seed, int nthreads = 0);
 
 // R-MAT graph with 2^scale vertices: `edges` samples with quadrant probabilities
 // (a, b, c, 1-a-b-c), duplicates removed, values U(-1,1).
-CSR gen_rmat(int scale, int64_t edges, double a, double b, double c, uint64_t seed, int nthreads = 0);
+VCSRMC_CXX_API CSR gen_rmat(int scale, int64_t edges, double a, double b, double c, uint64_t seed, int nthreads = 0);
 
 // rows x cols row-major U(-1,1), element i = row * cols + col of the dense stream.
-void gen_dense(int64_t rows, int cols, uint64_t seed, float* out, int nthreads = 0);
+VCSRMC_CXX_API void gen_dense(int64_t rows, int cols, uint64_t seed, float* out, int nthreads = 0);
 
-int poisson_inverse(double u, double lambda, int cap);
+VCSRMC_CXX_API int poisson_inverse(double u, double lambda, int cap);
 
 // P+1 nnz-balanced row cuts: cuts[k] = first row whose nnz prefix reaches ceil(k*nnz/P).
-std::vector<int> partition_rows(const int* row_ptr, int M, int parts);
+VCSRMC_CXX_API std::vector<int> partition_rows(const int* row_ptr, int M, int parts);
 
 }  // namespace vcsrmc

@@ -14,6 +14,10 @@
 #include <vector>
 #include "csr.hpp"
 
+#ifndef VCSRMC_CXX_API
+#define VCSRMC_CXX_API __attribute__((visibility("default")))
+#endif
+
 namespace vcsrmc {
 
 struct VCSRMC {
@@ -26,10 +30,10 @@ struct VCSRMC {
 };
 
 // Factor that A is divided by before FP16 conversion (C is multiplied back by it).
-float half_scale(const CSR& csr);
+VCSRMC_CXX_API float half_scale(const CSR& csr);
 
 // segw must be 16, 32, 48 or 64. `nthreads` <= 0 picks the hardware concurrency; the result
 // does not depend on it.
-VCSRMC csr_to_vcsr_mc(const CSR& csr, bool fp32 = false, int segw = 16, int nthreads = 0);
+VCSRMC_CXX_API VCSRMC csr_to_vcsr_mc(const CSR& csr, bool fp32 = false, int segw = 16, int nthreads = 0);
 
 }  // namespace vcsrmc

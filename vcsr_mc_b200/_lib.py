@@ -75,6 +75,7 @@ PROTOTYPES = {
     "vcsrmc_build_host": (_int, [_p, _int, _int, _int, _pp]),
     "vcsrmc_format_view_get": (_int, [_p, ctypes.POINTER(FormatView)]),
     "vcsrmc_format_free": (None, [_p]),
+    "vcsrmc_format_from_view": (_int, [ctypes.POINTER(FormatView), _pp]),
     "vcsrmc_upload": (_int, [_p, _int, _p, _pp]),
     "vcsrmc_upload_ex": (_int, [_p, _int, _int, _p, _pp]),
     "vcsrmc_device_free": (_int, [_p]),

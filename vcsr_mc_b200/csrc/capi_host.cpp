@@ -185,6 +185,42 @@ VCSRMC_EXPORT int vcsrmc_format_view_get(const vcsrmc_format* f, vcsrmc_format_v
     });
 }
 
+VCSRMC_EXPORT int vcsrmc_format_from_view(const vcsrmc_format_view* in, vcsrmc_format** out) {
+    return guarded([&] {
+        if (!in || !out || in->n_groups < 0 || in->n_slots < 0 || in->n_items < 0 || in->M < 0 || in->N < 0)
+            throw StatusError(VCSRMC_INVALID_ARG, "bad format view");
+        auto need = [](const void* p, int64_t n) {
+            if (n > 0 && !p) throw StatusError(VCSRMC_INVALID_ARG, "NULL array in format view");
+        };
+        need(in->group_ptr, in->n_groups + 1);
+        need(in->group_depth, in->n_groups);
+        need(in->group_seg_base, in->n_groups);
+        need(in->group_rows, 16 * in->n_groups);
+        need(in->lcol, in->n_slots);
+        need(in->val, in->n_slots);
+        need(in->item_gbeg, in->n_items);
+        need(in->item_gend, in->n_items);
+        auto* f = new vcsrmc_format;
+        VCSRMC& v = f->v;
+        v.M = in->M;
+        v.N = in->N;
+        v.segw = in->segw;
+        v.bundle = in->bundle;
+        v.num_segments = in->num_segments;
+        v.fp32 = in->fp32 != 0;
+        v.scale = in->scale;
+        v.group_ptr.assign(in->group_ptr, in->group_ptr + in->n_groups + 1);
+        v.group_depth.assign(in->group_depth, in->group_depth + in->n_groups);
+        v.group_seg_base.assign(in->group_seg_base, in->group_seg_base + in->n_groups);
+        v.group_rows.assign(in->group_rows, in->group_rows + 16 * in->n_groups);
+        v.lcol.assign(in->lcol, in->lcol + in->n_slots);
+        v.val.assign(in->val, in->val + in->n_slots);
+        v.item_gbeg.assign(in->item_gbeg, in->item_gbeg + in->n_items);
+        v.item_gend.assign(in->item_gend, in->item_gend + in->n_items);
+        *out = f;
+    });
+}
+
 VCSRMC_EXPORT void vcsrmc_format_free(vcsrmc_format* f) { delete f; }
 
 VCSRMC_EXPORT int vcsrmc_gen_csr(int kind, int32_t param, uint64_t seed, int nthreads, vcsrmc_csr** out) {

@@ -255,6 +255,7 @@ VCSRMC_EXPORT int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans
             throw StatusError(VCSRMC_INVALID_ARG, "unknown plan bits");
         const VCSRMC& v = f->v;
         validate_format(v);
+        if (device < 0) cuda_check(cudaGetDevice(&device), "cudaGetDevice");
         DeviceGuard guard(device);
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         auto* d = new vcsrmc_device_format;
