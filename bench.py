@@ -201,6 +201,34 @@ def time_reference_cpu(M, N, rp, col, val, steps: int, warmup: int, target_nnz: 
             "ms_per_step": dt * 1e3}
 
 
+def time_cusparse(rp, col, val, r0, r1, p0, p1, N, B, fp16: bool, stream) -> dict:
+    """cuSPARSE CSR SpMM (libvcsrmc_cusparse.so) on this rank's rows and the same device B:
+    FP16 A/B with FP32 compute and C for the FP16 path, FP32 otherwise. Median of 10 launches."""
+    import ctypes
+    import torch
+    path = os.path.join(ROOT, "vcsr_mc_b200", "libvcsrmc_cusparse.so")
+    if not os.path.exists(path):
+        return {"unavailable": "libvcsrmc_cusparse.so not built"}
+    lib = ctypes.CDLL(path)
+    lib.vcsrmc_cusparse_last_error.restype = ctypes.c_char_p
+    d_rp = torch.from_numpy(np.asarray(rp[r0:r1 + 1], dtype=np.int64) - p0).to(torch.int32).cuda()
+    d_col = torch.from_numpy(np.asarray(col[p0:p1], dtype=np.int32)).cuda()
+    v = torch.from_numpy(np.asarray(val[p0:p1], dtype=np.float32)).cuda()
+    d_val = v.half() if fp16 else v
+    C = torch.empty((max(r1 - r0, 1), B.shape[1]), dtype=torch.float32, device="cuda")
+    ms = ctypes.c_float()
+    rc = lib.vcsrmc_cusparse_spmm(ctypes.c_int32(r1 - r0), ctypes.c_int32(N), ctypes.c_int64(p1 - p0),
+                                  ctypes.c_void_p(d_rp.data_ptr()), ctypes.c_void_p(d_col.data_ptr()),
+                                  ctypes.c_void_p(d_val.data_ptr()), 1 if fp16 else 0, ctypes.c_void_p(B.data_ptr()),
+                                  1 if fp16 else 0, ctypes.c_int32(B.shape[1]), ctypes.c_void_p(C.data_ptr()),
+                                  ctypes.c_float(1.0), 3, 10, ctypes.c_void_p(stream.cuda_stream), ctypes.byref(ms))
+    if rc != 0:
+        return {"unavailable": lib.vcsrmc_cusparse_last_error().decode()}
+    nnz = p1 - p0
+    return {"algo": "cusparseSpMM CSR_ALG_DEFAULT " + ("fp16 A/B, fp32 C" if fp16 else "fp32"),
+            "ms": ms.value, "gflops": 2.0 * nnz * B.shape[1] / (ms.value * 1e6), "rows": r1 - r0, "nnz": nnz}
+
+
 # ---------------------------------------------------------------------------------------------
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -217,6 +245,7 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cusparse", action="store_true")
     ap.add_argument("--cpu-sample-nnz", type=int, default=8_000_000)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -371,6 +400,10 @@ def main() -> None:
                "h2d_bytes_per_step": int(hB.numel() * hB.element_size()),
                "d2h_bytes_per_step": int(hC.numel() * hC.element_size()), "ms_per_step": float(e2e_ms)}
 
+    cusparse = None
+    if rank == 0 and not args.no_cusparse:
+        cusparse = time_cusparse(rp, col, val, r0, r1, p0, p1, N, B, fp16, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -392,7 +425,7 @@ def main() -> None:
                                     "vcsr_mc_fp16_tc_kernel" if fp16 else "vcsr_mc_fp32_kernel"),
                          "kernel_ms": kern_ms, "kernel_ms_max_over_ranks": kern_max_ms,
                          "algorithmic_bytes": bytes_alg},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps * (2 if args.plan == "rows" else 1),
+            "cpu_baseline": cpu, "e2e": e2e, "cusparse": cusparse, "gpu_launches": args.steps * (2 if args.plan == "rows" else 1),
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "detail": {"nnz": nnz_total, "M": M, "N": N, "rank0_rows": Ms, "rank0_distinct_cols": D,
                        "groups": groups, "slots": slots, "items": items, "device_status": status,
