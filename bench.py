@@ -27,6 +27,12 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+_RESULT_FD = 1
+
+
+def emit(obj: dict) -> None:
+    """Writes the single JSON result line to the original stdout."""
+    os.write(_RESULT_FD, (json.dumps(obj) + "\n").encode())
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
@@ -212,8 +218,8 @@ def time_cusparse(rp, col, val, r0, r1, p0, p1, N, B, fp16: bool, stream) -> dic
     lib = ctypes.CDLL(path)
     lib.vcsrmc_cusparse_last_error.restype = ctypes.c_char_p
     d_rp = torch.from_numpy(np.asarray(rp[r0:r1 + 1], dtype=np.int64) - p0).to(torch.int32).cuda()
-    d_col = torch.from_numpy(np.asarray(col[p0:p1], dtype=np.int32)).cuda()
-    v = torch.from_numpy(np.asarray(val[p0:p1], dtype=np.float32)).cuda()
+    d_col = torch.from_numpy(np.array(col[p0:p1], dtype=np.int32)).cuda()
+    v = torch.from_numpy(np.array(val[p0:p1], dtype=np.float32)).cuda()
     d_val = v.half() if fp16 else v
     C = torch.empty((max(r1 - r0, 1), B.shape[1]), dtype=torch.float32, device="cuda")
     ms = ctypes.c_float()
@@ -231,6 +237,12 @@ def time_cusparse(rp, col, val, r0, r1, p0, p1, N, B, fp16: bool, stream) -> dic
 
 # ---------------------------------------------------------------------------------------------
 def main() -> None:
+    # Only the result line goes to stdout: everything else (libraries included, e.g. NCCL's
+    # version banner) is sent to stderr at the file-descriptor level.
+    result_fd = os.dup(1)
+    os.dup2(2, 1)
+    global _RESULT_FD
+    _RESULT_FD = result_fd
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
@@ -247,6 +259,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
     ap.add_argument("--cpu-sample-nnz", type=int, default=8_000_000)
+    ap.add_argument("--row-weight", type=float, default=5.4,
+                    help="shard balance: cost = nnz + row_weight * rows (0 = nnz balance)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -259,7 +273,7 @@ def main() -> None:
               "path": (("fp16 A/B, fp32 accumulate, " if fp16 else "fp32, ") +
                        ("CUDA-core FFMA" if (args.plan == "rows" or not fp16) else "tcgen05 MMA, TMEM accumulator")), "plan": {"rows": "rows: row-stationary over the VCSR-MC row view, C stored once",
                        "segment": "segment: reference dataflow, per-item B segment, C reductions"}[args.plan],
-              "parallelism": f"row-shard x{args.gpus} (nnz-balanced), B replicated",
+              "parallelism": f"row-shard x{args.gpus} (balanced on nnz + {args.row_weight} x rows), B replicated",
               "l2": "inputs larger than L2 (no flush needed)"}
 
     if args.impl == "reference":
@@ -270,15 +284,15 @@ def main() -> None:
             M, N, rp, col, val = load_or_generate_csr(spec, 0, 1, lambda: None)
             cb = time_reference_cpu(M, N, rp, col, val, args.steps, args.warmup, args.cpu_sample_nnz, fp16)
         except Exception as e:  # noqa: BLE001
-            print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"}))
+            emit({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"})
             return
-        print(json.dumps({
+        emit({
             "impl": "reference", "metric": "SpMM effective GFLOP/s (2*nnz*N/t)", "value": cb["value"],
             "unit": "GFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f64" , "data": "synthetic", "config": config,
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": cb["value"], "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+            "e2e": {"value": cb["value"], "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return
 
     import torch
@@ -299,7 +313,7 @@ def main() -> None:
     t0 = time.time()
     M, N, rp, col, val = load_or_generate_csr(spec, rank, world, barrier)
     nnz_total = int(rp[M])
-    cuts = vm.partition_rows(np.asarray(rp, dtype=np.int32), world)
+    cuts = vm.partition_rows(np.asarray(rp, dtype=np.int32), world, row_weight=args.row_weight)
     r0, r1 = int(cuts[rank]), int(cuts[rank + 1])
     p0, p1 = int(rp[r0]), int(rp[r1])
     shard = vm.CSR.from_arrays(r1 - r0, N, np.asarray(rp[r0:r1 + 1], dtype=np.int64) - p0,
@@ -431,7 +445,7 @@ def main() -> None:
                        "groups": groups, "slots": slots, "items": items, "device_status": status,
                        "clock_samples": clk["samples"]},
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     dV.free()
     if dist is not None:
         dist.barrier()

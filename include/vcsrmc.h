@@ -170,6 +170,10 @@ int vcsrmc_gen_dense_device(int64_t rows, int32_t cols, uint64_t seed, int dtype
 /* ---- multi-GPU row partition (no reference counterpart) --------------------------------
  * cuts[0..parts]: cuts[k] = first row whose nnz prefix reaches ceil(k * nnz / parts). */
 int vcsrmc_partition_rows(const int32_t* row_ptr, int32_t M, int32_t parts, int32_t* cuts);
+/* Same, balancing nnz + row_weight * rows per block (each output row also costs a C row store;
+ * row_weight = 0 is the nnz balance above). */
+int vcsrmc_partition_rows_weighted(const int32_t* row_ptr, int32_t M, int32_t parts, double row_weight,
+                                   int32_t* cuts);
 
 #ifdef __cplusplus
 }

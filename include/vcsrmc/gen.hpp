@@ -37,5 +37,8 @@ VCSRMC_CXX_API int poisson_inverse(double u, double lambda, int cap);
 
 // P+1 nnz-balanced row cuts: cuts[k] = first row whose nnz prefix reaches ceil(k*nnz/P).
 VCSRMC_CXX_API std::vector<int> partition_rows(const int* row_ptr, int M, int parts);
+// P+1 row cuts balancing the cost nnz + row_weight * rows of each block: cuts[k] = first row r
+// whose prefix cost row_ptr[r] + row_weight * r reaches k/P of the total.
+VCSRMC_CXX_API std::vector<int> partition_rows_weighted(const int* row_ptr, int M, int parts, double row_weight);
 
 }  // namespace vcsrmc

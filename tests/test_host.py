@@ -295,3 +295,17 @@ def test_partition_rows():
         for k in range(1, parts):
             target = -(-k * A.nnz // parts)
             assert rp[cuts[k]] >= target and (cuts[k] == 0 or rp[cuts[k] - 1] < target)
+
+
+def test_partition_rows_weighted():
+    A = vm.CSR.generate(vm.GEN_RMAT, 14, seed=3)
+    rp, _, _ = A.arrays()
+    w = 5.4
+    for parts in (2, 4, 8):
+        cuts = vm.partition_rows(rp, parts, row_weight=w)
+        assert cuts[0] == 0 and cuts[-1] == A.M and np.all(np.diff(cuts) >= 0)
+        cost = rp.astype(np.float64) + w * np.arange(A.M + 1)
+        for k in range(1, parts):
+            target = cost[-1] * k / parts
+            assert cost[cuts[k]] >= target and (cuts[k] == 0 or cost[cuts[k] - 1] < target)
+    assert np.array_equal(vm.partition_rows(rp, 4, row_weight=0.0), vm.partition_rows(rp, 4))

@@ -87,6 +87,7 @@ PROTOTYPES = {
     "vcsrmc_gen_dense_host": (_int, [_i64, _i32, _u64, _p, _int]),
     "vcsrmc_gen_dense_device": (_int, [_i64, _i32, _u64, _int, _p, _i64, _p]),
     "vcsrmc_partition_rows": (_int, [_p, _i32, _i32, _p]),
+    "vcsrmc_partition_rows_weighted": (_int, [_p, _i32, _i32, ctypes.c_double, _p]),
 }
 
 _lib = None

@@ -277,8 +277,12 @@ def gen_dense_device(out, seed: int, stream=None):
     return out
 
 
-def partition_rows(row_ptr: np.ndarray, parts: int) -> np.ndarray:
+def partition_rows(row_ptr: np.ndarray, parts: int, row_weight: float = 0.0) -> np.ndarray:
+    """parts+1 row cuts balancing nnz + row_weight * rows per block (0: pure nnz balance)."""
     rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
     cuts = np.empty(parts + 1, dtype=np.int32)
-    call("vcsrmc_partition_rows", _ptr(rp), int(rp.size - 1), parts, _ptr(cuts))
+    if row_weight == 0.0:
+        call("vcsrmc_partition_rows", _ptr(rp), int(rp.size - 1), parts, _ptr(cuts))
+    else:
+        call("vcsrmc_partition_rows_weighted", _ptr(rp), int(rp.size - 1), parts, float(row_weight), _ptr(cuts))
     return cuts

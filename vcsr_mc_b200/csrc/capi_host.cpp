@@ -267,3 +267,12 @@ VCSRMC_EXPORT int vcsrmc_partition_rows(const int32_t* row_ptr, int32_t M, int32
         std::copy(c.begin(), c.end(), cuts);
     });
 }
+
+VCSRMC_EXPORT int vcsrmc_partition_rows_weighted(const int32_t* row_ptr, int32_t M, int32_t parts, double row_weight,
+                                                 int32_t* cuts) {
+    return guarded([&] {
+        if (!row_ptr || !cuts || M < 0 || parts < 1) throw StatusError(VCSRMC_INVALID_ARG, "bad partition arguments");
+        const std::vector<int> c = partition_rows_weighted(row_ptr, M, parts, row_weight);
+        std::copy(c.begin(), c.end(), cuts);
+    });
+}

@@ -292,4 +292,20 @@ std::vector<int> partition_rows(const int* row_ptr, int M, int parts) {
     return cuts;
 }
 
+std::vector<int> partition_rows_weighted(const int* row_ptr, int M, int parts, double row_weight) {
+    if (parts < 1 || M < 0 || !(row_weight >= 0)) throw std::runtime_error("bad partition request");
+    std::vector<int> cuts(size_t(parts) + 1, 0);
+    const double base = row_ptr[0];
+    const double total = (double(row_ptr[M]) - base) + row_weight * M;
+    cuts[parts] = M;
+    int r = 0;
+    for (int k = 1; k < parts; ++k) {
+        const double target = total * k / parts;
+        // the prefix cost is non-decreasing in r: advance to the first row that reaches the target
+        while (r < M && (double(row_ptr[r]) - base) + row_weight * r < target) ++r;
+        cuts[k] = std::max(cuts[k - 1], r);
+    }
+    return cuts;
+}
+
 }  // namespace vcsrmc
