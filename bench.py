@@ -387,6 +387,14 @@ def main() -> None:
             peak = float(json.load(f)["hbm_gbs"])
         peak_src = "measured (MEASURED_PEAKS.json hbm_gbs)"
     achieved = bytes_alg / (kern_ms * 1e-3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "measured_traffic.json")
+    tkey = f"{args.workload}{args.scale if args.workload == 'rmat' else ''}/{args.dtype}/{args.plan}"
+    if world == 1 and os.path.exists(tpath):
+        with open(tpath) as f:
+            rec = json.load(f).get(tkey)
+        if rec:
+            traffic = rec["dram_bytes_read"] + rec["dram_bytes_write"]
 
     # end to end through the C ABI with host buffers: H2D of B (pinned), zero C, SpMM, D2H of C
     e2e = None
@@ -434,7 +442,9 @@ def main() -> None:
             "data": "synthetic (seeded generator, seed 0)",
             "config": config,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                           "(profiles/measured_traffic.json)" if traffic else None,
                          "kernel": ("vcsr_rows_kernel" if args.plan == "rows" else
                                     "vcsr_mc_fp16_tc_kernel" if fp16 else "vcsr_mc_fp32_kernel"),
                          "kernel_ms": kern_ms, "kernel_ms_max_over_ranks": kern_max_ms,
