@@ -37,6 +37,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 O_COLS = 128
+L2_BYTES = 126 * (1 << 20)
 SEED = 0
 CACHE_DIR = os.environ.get("VCSRMC_BENCH_CACHE", "/dev/shm/vcsrmc_bench")
 
@@ -253,12 +254,14 @@ def main() -> None:
     ap.add_argument("--dtype", choices=["fp16", "fp32"], default="fp16")
     ap.add_argument("--segw", type=int, default=32)
     ap.add_argument("--tileK", type=int, default=128)
-    ap.add_argument("--plan", choices=["rows", "segment"], default="rows")
+    ap.add_argument("--plan", choices=["rows", "segment", "band"], default="rows")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
     ap.add_argument("--cpu-sample-nnz", type=int, default=8_000_000)
+    ap.add_argument("--unit-nnz", type=int, default=0,
+                    help="ROWS plan: entries per work unit (0 = the library's choice for the matrix)")
     ap.add_argument("--row-weight", type=float, default=5.4,
                     help="shard balance: cost = nnz + row_weight * rows (0 = nnz balance)")
     args = ap.parse_args()
@@ -271,10 +274,12 @@ def main() -> None:
     fp16 = args.dtype == "fp16"
     config = {"workload": spec["desc"], "O": O_COLS, "segw": args.segw, "tileK": args.tileK,
               "path": (("fp16 A/B, fp32 accumulate, " if fp16 else "fp32, ") +
-                       ("CUDA-core FFMA" if (args.plan == "rows" or not fp16) else "tcgen05 MMA, TMEM accumulator")), "plan": {"rows": "rows: row-stationary over the VCSR-MC row view, C stored once",
-                       "segment": "segment: reference dataflow, per-item B segment, C reductions"}[args.plan],
+                       ("CUDA-core FFMA" if (args.plan == "rows" or not fp16) else "tcgen05 MMA, TMEM accumulator")),
+              "plan": {"rows": "rows: row-stationary over the VCSR-MC row view, C stored once",
+                       "segment": "segment: reference dataflow, per-item B segment, C reductions",
+                       "band": "band: 128-row bands x 32-column tiles on tcgen05, TMEM accumulator, C stored once"}[args.plan],
               "parallelism": f"row-shard x{args.gpus} (balanced on nnz + {args.row_weight} x rows), B replicated",
-              "l2": "inputs larger than L2 (no flush needed)"}
+              "l2": None}
 
     if args.impl == "reference":
         # The reference's own CPU implementation of the path (oracle/_ref), rank 0 only.
@@ -323,9 +328,13 @@ def main() -> None:
     V = vm.csr_to_vcsr_mc(shard, fp32=not fp16, segw=args.segw, nthreads=nthreads)
     build_s = time.time() - tb
     D = int(np.unique(np.asarray(col[p0:p1])).size) if p1 > p0 else 0
-    plan = vm.PLAN_ROWS if args.plan == "rows" else vm.PLAN_SEGMENT
-    dV = vm.upload_vcsr_mc_device(V, device=local, plans=[plan])
+    plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND}[args.plan]
+    dV = vm.upload_vcsr_mc_device(V, device=local, plans=[plan], rows_unit_nnz=args.unit_nnz)
     Ms = r1 - r0
+    # this library's kernels per step: the SpMM kernel, plus (ROWS plan) the zeroing of rows
+    # longer than one 256-entry work unit, whose chunks are reduced into C
+    heavy = int(np.count_nonzero(np.diff(np.asarray(rp[r0:r1 + 1], dtype=np.int64)) > 256))
+    launches_per_step = 1 + (1 if plan == vm.PLAN_ROWS and heavy > 0 else 0)
     groups, slots, items = V.n_groups, V.n_slots, V.n_items
     del V
     log(f"rank {rank}: rows [{r0},{r1}) nnz {p1 - p0} groups {groups} slots {slots} items {items} "
@@ -336,8 +345,20 @@ def main() -> None:
     vm.gen_dense_device(B, SEED)
     C = torch.empty((max(Ms, 1), O_COLS), dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream()
+    # Inputs that do not dwarf the L2 would be served from it on the next step: flush it by
+    # writing a buffer twice its size before every step and time only the SpMM call (per-step
+    # events on the launching stream).
+    s_ab = 2 if fp16 else 4
+    footprint = (p1 - p0) * (4 + s_ab) + (Ms + 1) * 4 + N * O_COLS * s_ab + Ms * O_COLS * 4
+    flush = footprint < 4 * L2_BYTES
+    l2buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda") if flush else None
+    config["l2"] = (f"footprint {footprint / 1e6:.0f} MB < 4 x L2: L2 flushed (write of {2 * L2_BYTES >> 20} MiB) "
+                    "before every step; time = per-step CUDA events around the SpMM call" if flush else
+                    f"footprint {footprint / 1e9:.2f} GB, larger than L2 (126 MB): no flush; time = K back-to-back steps")
 
-    def step(ev_k0=None, ev_k1=None):
+    def step(ev_k0=None, ev_k1=None, i=0):
+        if flush:
+            l2buf.fill_(i & 0xff)
         # ROWS plan: every C row is stored once, so no zeroing pass; SEGMENT plan: C += A*B
         # through reductions needs C zeroed first (the reference's caller does the same).
         if plan == vm.PLAN_SEGMENT:
@@ -360,7 +381,7 @@ def main() -> None:
     torch.cuda.synchronize()
     start.record(stream)
     for i in range(args.steps):
-        step(*kev[i])
+        step(*kev[i], i=i)
     stop.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -373,12 +394,11 @@ def main() -> None:
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms, kern_max_ms = float(t[0]), float(t[1])
-    ms_per_step = total_ms / args.steps
+    ms_per_step = kern_max_ms if flush else total_ms / args.steps
     flops = 2.0 * nnz_total * O_COLS
     value = flops / (ms_per_step * 1e-3) / 1e9
 
     # roofline of the SpMM kernel on this rank (algorithmic bytes of this rank's launch)
-    s_ab = 2 if fp16 else 4
     bytes_alg = algorithmic_bytes(p1 - p0, Ms, D, O_COLS, s_ab)
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak, peak_src = 6650.0, "fallback 6.65 TB/s"
@@ -445,11 +465,11 @@ def main() -> None:
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
                                            "(profiles/measured_traffic.json)" if traffic else None,
-                         "kernel": ("vcsr_rows_kernel" if args.plan == "rows" else
-                                    "vcsr_mc_fp16_tc_kernel" if fp16 else "vcsr_mc_fp32_kernel"),
+                         "kernel": {"rows": "vcsr_rows_kernel", "band": "vcsr_band_kernel",
+                                    "segment": "vcsr_mc_fp16_tc_kernel" if fp16 else "vcsr_mc_fp32_kernel"}[args.plan],
                          "kernel_ms": kern_ms, "kernel_ms_max_over_ranks": kern_max_ms,
                          "algorithmic_bytes": bytes_alg},
-            "cpu_baseline": cpu, "e2e": e2e, "cusparse": cusparse, "gpu_launches": args.steps * (2 if args.plan == "rows" else 1),
+            "cpu_baseline": cpu, "e2e": e2e, "cusparse": cusparse, "gpu_launches": args.steps * launches_per_step,
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "detail": {"nnz": nnz_total, "M": M, "N": N, "rank0_rows": Ms, "rank0_distinct_cols": D,
                        "groups": groups, "slots": slots, "items": items, "device_status": status,

@@ -47,10 +47,14 @@ extern "C" {
  *          segment once, multiply every 16-row group, add it into C with reductions.
  * ROWS:    row-stationary over the format's row view (built at upload): each C row is
  *          accumulated in registers from gathered B rows and stored once.
- * AUTO:    ROWS when its layout is resident, else SEGMENT.                                */
+ * BAND:    FP16 format only: bands of 128 rows, tiles of 32 columns multiplied on the tensor
+ *          cores into one accumulator per band, C stored once. For matrices whose rows touch
+ *          few column windows (stencils, banded or reordered matrices).
+ * AUTO:    BAND, ROWS, SEGMENT: the first whose layout is resident.                        */
 #define VCSRMC_PLAN_AUTO 0
 #define VCSRMC_PLAN_SEGMENT 1
 #define VCSRMC_PLAN_ROWS 2
+#define VCSRMC_PLAN_BAND 3
 
 /* ---- synthetic configurations (vcsrmc_gen_csr) ---------------------------------------- */
 #define VCSRMC_GEN_UNIFORM_POISSON 1 /* param: M = N; mean row length 16                   */
@@ -130,10 +134,21 @@ void vcsrmc_format_free(vcsrmc_format* f);
  * calling thread's current device) in the kernels' layout (FP16 formats keep fp16 values on
  * the device). Blocking. */
 int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out);
-/* Same, choosing which plan layouts to make resident: a bit mask of (1 << VCSRMC_PLAN_SEGMENT)
- * and (1 << VCSRMC_PLAN_ROWS); 0 = all (what vcsrmc_upload does). */
+/* Same, choosing which plan layouts to make resident: a bit mask of (1 << VCSRMC_PLAN_SEGMENT),
+ * (1 << VCSRMC_PLAN_ROWS) and (1 << VCSRMC_PLAN_BAND); 0 = SEGMENT and ROWS (what vcsrmc_upload
+ * does). */
 int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans, void* stream,
                      vcsrmc_device_format** out);
+/* Upload tuning; zero-initialise and set what you need (0 = the library's choice). */
+typedef struct {
+    int32_t plans;         /* plan layouts to make resident, as in vcsrmc_upload_ex           */
+    int32_t rows_unit_nnz; /* ROWS plan: entries per work unit, a power of two in [16, 1024];
+                              rows with more entries are split into chunks of this size.
+                              0 = chosen from the matrix so that every SM gets enough units.  */
+    int32_t reserved[6];   /* must be 0                                                        */
+} vcsrmc_upload_options;
+int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const vcsrmc_upload_options* opts,
+                       void* stream, vcsrmc_device_format** out);
 int vcsrmc_device_free(vcsrmc_device_format* d);
 /* Error flags raised by kernels of this format since the last clear (bit 0: a bounded wait
  * timed out). Blocking read. */

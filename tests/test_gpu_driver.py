@@ -18,9 +18,9 @@ def run_driver(*args):
     return list(csv.DictReader(io.StringIO(out.stdout)))
 
 
-@pytest.mark.parametrize("extra", [[], ["--plan", "segment"], ["--plan", "rows", "--b16"], ["--reorder", "rcm"],
-                                   ["--bdist", "wide", "--segw", "32", "--tileK", "128"]],
-                         ids=["reference-call", "segment", "rows-b16", "rcm", "wide-s32-t128"])
+@pytest.mark.parametrize("extra", [[], ["--plan", "segment"], ["--plan", "rows", "--b16"], ["--plan", "band", "--b16"],
+                                   ["--reorder", "rcm"], ["--bdist", "wide", "--segw", "32", "--tileK", "128"]],
+                         ids=["reference-call", "segment", "rows-b16", "band-b16", "rcm", "wide-s32-t128"])
 def test_driver_all_algorithms_pass(extra):
     rows = run_driver("--gen", "c1", "--algo", "all", "--repeat", "2", "--warmup", "1", *extra)
     algos = {r["algo"]: r for r in rows}

@@ -15,16 +15,19 @@ from tests.helpers import check_fp16, check_fp32, random_csr
 pytestmark = pytest.mark.gpu
 
 
-PLANS = [vm.PLAN_SEGMENT, vm.PLAN_ROWS]
-PLAN_IDS = ["segment", "rows"]
+PLANS = [vm.PLAN_SEGMENT, vm.PLAN_ROWS, vm.PLAN_BAND]
+PLAN_IDS = ["segment", "rows", "band"]
 
 
 def run_gpu(torch, A: vm.CSR, B32: np.ndarray, fp32: bool, segw: int, tileK: int, b_half: bool,
-            accumulate_into=None, ldb_pad: int = 0, ldc_pad: int = 0, plan: int = vm.PLAN_SEGMENT):
+            accumulate_into=None, ldb_pad: int = 0, ldc_pad: int = 0, plan: int = vm.PLAN_SEGMENT,
+            unit_nnz: int = 0):
     """C = A*B (or C = accumulate_into + A*B) on cuda:0 with one plan; returns (C, B values used)."""
+    if plan == vm.PLAN_BAND and fp32:
+        pytest.skip("the BAND plan runs on the tensor cores: FP16 format only")
     O = B32.shape[1]
     V = vm.csr_to_vcsr_mc(A, fp32=fp32, segw=segw)
-    dV = vm.upload_vcsr_mc_device(V, device=0, plans=[plan])
+    dV = vm.upload_vcsr_mc_device(V, device=0, plans=[plan], rows_unit_nnz=unit_nnz)
     dt = torch.float16 if b_half else torch.float32
     Bfull = torch.zeros((B32.shape[0], O + ldb_pad), dtype=dt, device="cuda")
     Bfull[:, :O] = torch.from_numpy(B32).to(device="cuda", dtype=dt)
@@ -86,6 +89,19 @@ def test_zipf_power_law(cuda, plan, fp32):
     B = vm.gen_dense_host(1 << 16, 128, seed=0)
     C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32, plan=plan)
     oracle_check(A, C, Bu, fp32)
+
+
+@pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
+@pytest.mark.parametrize("unit_nnz", [16, 64, 1024])
+@pytest.mark.parametrize("accumulate", [False, True], ids=["store", "accumulate"])
+def test_rows_unit_sizes(cuda, unit_nnz, fp32, accumulate):
+    """ROWS plan work units of 16 .. 1024 entries: heavy rows split into many or few chunks."""
+    A = vm.CSR.generate(vm.GEN_ZIPF, 1 << 14, seed=5)
+    B = vm.gen_dense_host(1 << 14, 128, seed=5)
+    base = np.random.default_rng(6).uniform(-1, 1, size=(A.M, 128)).astype(np.float32) if accumulate else None
+    C, Bu = run_gpu(cuda, A, B, fp32, 32, 128, b_half=not fp32, accumulate_into=base, plan=vm.PLAN_ROWS,
+                    unit_nnz=unit_nnz)
+    oracle_check(A, C, Bu, fp32, base=None if base is None else base.astype(np.float64))
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
@@ -199,6 +215,41 @@ def test_dense_device_generator_matches_host(cuda):
     torch.cuda.synchronize()
     assert np.array_equal(d32.cpu().numpy(), h)
     assert np.array_equal(d16.cpu().numpy(), h.astype(np.float16))
+
+
+@pytest.mark.parametrize("n", [1, 100, 128, 129, 300])
+def test_band_plan_shapes(cuda, n):
+    """BAND plan: partial last band, bands without entries, tiles at the last columns, N < 32."""
+    rp, col, val = random_csr(n, n, min(1.0, 6.0 / n), seed=n, empty_rows=True)
+    A = vm.CSR.from_arrays(n, n, rp, col, val)
+    B = np.random.default_rng(n).uniform(-1, 1, size=(n, 128)).astype(np.float32)
+    C, Bu = run_gpu(cuda, A, B, False, 32, 128, b_half=True, plan=vm.PLAN_BAND)
+    oracle_check(A, C, Bu, False)
+
+
+def test_band_plan_needs_fp16_format(cuda):
+    A = vm.CSR.generate(vm.GEN_UNIFORM_POISSON, 256, seed=1)
+    with pytest.raises(vm.VcsrmcError) as e:
+        vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=True, segw=32), plans=[vm.PLAN_BAND])
+    assert e.value.status == 1 and "FP16" in str(e.value)
+
+
+def test_auto_plan_prefers_band_when_resident(cuda):
+    torch = cuda
+    A = vm.CSR.generate(vm.GEN_STENCIL27, 16, seed=0)
+    B32 = vm.gen_dense_host(A.N, 128, seed=2)
+    dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=False, segw=32), plans=[vm.PLAN_BAND])
+    B = torch.from_numpy(B32).cuda().half()
+    C = torch.full((A.M, 128), 5.0, device="cuda")
+    vm.spmm(dV, B, C, accumulate=False)  # AUTO -> BAND, the only resident layout
+    torch.cuda.synchronize()
+    rp, col, val = A.arrays()
+    ref, ab = ob.spmm_fp64(rp, col, val, B.float().cpu().numpy(), with_abs=True)
+    check_fp16(C.cpu().numpy(), ref, ab)
+    assert dV.status() == 0
+    with pytest.raises(vm.VcsrmcError):
+        vm.spmm(dV, B, C, plan=vm.PLAN_ROWS)  # not uploaded
+    dV.free()
 
 
 def test_errors_are_status_codes(cuda):

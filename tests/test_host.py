@@ -50,6 +50,15 @@ def test_status_codes_and_messages():
     with pytest.raises(vm.VcsrmcError) as e:
         vm.read_matrix_market("/nonexistent/file.mtx")
     assert e.value.status == 5
+    # upload options are checked before any device work
+    import ctypes
+    V = vm.csr_to_vcsr_mc(A, segw=32)
+    for bad in (8, 48, 2048):
+        opts = vm._lib.UploadOptions()
+        opts.rows_unit_nnz = bad
+        with pytest.raises(vm.VcsrmcError) as e:
+            vm._lib.call("vcsrmc_upload_opts", V.handle, 0, ctypes.byref(opts), None, ctypes.byref(ctypes.c_void_p()))
+        assert e.value.status == 1 and "rows_unit_nnz" in str(e.value)
 
 
 # ---- builder ---------------------------------------------------------------------------------

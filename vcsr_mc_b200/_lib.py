@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(_HERE, "libvcsrmc.so")
 OK, INVALID_ARG, CUDA_ERR, OOM, TIMEOUT, IO_ERR, FORMAT_ERR, INTERNAL = range(8)
 F32, F16 = 0, 1
 GEN_UNIFORM_POISSON, GEN_ZIPF, GEN_STENCIL27, GEN_RMAT = 1, 2, 3, 4
-PLAN_AUTO, PLAN_SEGMENT, PLAN_ROWS = 0, 1, 2
+PLAN_AUTO, PLAN_SEGMENT, PLAN_ROWS, PLAN_BAND = 0, 1, 2, 3
 
 _STATUS_NAMES = {
     OK: "OK", INVALID_ARG: "INVALID_ARG", CUDA_ERR: "CUDA_ERR", OOM: "OOM", TIMEOUT: "TIMEOUT",
@@ -30,6 +30,10 @@ class VcsrmcError(RuntimeError):
     def __init__(self, status: int, message: str):
         self.status = status
         super().__init__(f"{_STATUS_NAMES.get(status, status)}: {message}")
+
+
+class UploadOptions(ctypes.Structure):
+    _fields_ = [("plans", ctypes.c_int32), ("rows_unit_nnz", ctypes.c_int32), ("reserved", ctypes.c_int32 * 6)]
 
 
 class CsrView(ctypes.Structure):
@@ -78,6 +82,7 @@ PROTOTYPES = {
     "vcsrmc_format_from_view": (_int, [ctypes.POINTER(FormatView), _pp]),
     "vcsrmc_upload": (_int, [_p, _int, _p, _pp]),
     "vcsrmc_upload_ex": (_int, [_p, _int, _int, _p, _pp]),
+    "vcsrmc_upload_opts": (_int, [_p, _int, ctypes.POINTER(UploadOptions), _p, _pp]),
     "vcsrmc_device_free": (_int, [_p]),
     "vcsrmc_device_status": (_int, [_p, ctypes.POINTER(ctypes.c_uint32), _int]),
     "vcsrmc_spmm": (_int, [_p, _p, _int, _i64, _i32, _i32, _p, _i64, _int, _p]),

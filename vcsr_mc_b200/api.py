@@ -213,12 +213,16 @@ class DeviceVCSRMC:
         return f.value
 
 
-def upload_vcsr_mc_device(V: VCSRMC, device: int = 0, stream=None, plans=None) -> DeviceVCSRMC:
-    """Copies the format to `device`. plans: iterable of PLAN_SEGMENT / PLAN_ROWS layouts to make
-    resident (default: both)."""
-    mask = 0 if plans is None else sum(1 << p for p in set(plans))
+def upload_vcsr_mc_device(V: VCSRMC, device: int = 0, stream=None, plans=None,
+                          rows_unit_nnz: int = 0) -> DeviceVCSRMC:
+    """Copies the format to `device`. plans: iterable of PLAN_SEGMENT / PLAN_ROWS / PLAN_BAND
+    layouts to make resident (default: SEGMENT and ROWS; BAND needs the FP16 format). rows_unit_nnz: entries per ROWS-plan work unit (0 = the library's
+    choice for this matrix)."""
+    opts = _lib.UploadOptions()
+    opts.plans = 0 if plans is None else sum(1 << p for p in set(plans))
+    opts.rows_unit_nnz = rows_unit_nnz
     h = ctypes.c_void_p()
-    call("vcsrmc_upload_ex", V.handle, device, mask, _stream_handle(stream), ctypes.byref(h))
+    call("vcsrmc_upload_opts", V.handle, device, ctypes.byref(opts), _stream_handle(stream), ctypes.byref(h))
     return DeviceVCSRMC(h, V, device)
 
 

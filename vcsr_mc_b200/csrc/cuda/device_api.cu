@@ -11,7 +11,9 @@
 //          (_Float16) conversion), fp32[n_slots] for the FP32 format
 //   status uint32           kernel error flags (bounded waits)
 // plus, for the ROWS plan (plan_rows.cu), the row view: rp int32[M+1], cols int32[nnz],
-//   vals fp16|fp32[nnz], units int4[n_units], split_rows int32[n_split_rows].
+//   vals fp16|fp32[nnz], units int4[n_units], split_rows int32[n_split_rows];
+// and for the BAND plan (plan_band.cu, FP16 format), the band view: tile_ptr int32[bands+1],
+//   tile_col int32[tiles], tile_eptr int32[tiles+1], ents uint32[nnz] (column, row, fp16 value).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -23,6 +25,7 @@
 #include "../common/vrng.h"
 #include "../host/parallel.hpp"
 #include "common.cuh"
+#include "plan_band.hpp"
 #include "plan_rows.hpp"
 #include "spmm_launch.hpp"
 
@@ -47,6 +50,14 @@ struct vcsrmc_device_format {
     void* rvals = nullptr;
     int* split_rows = nullptr;
     int n_split_rows = 0;
+    // BAND plan
+    bool has_band = false;
+    int n_bands = 0;
+    int64_t n_tiles = 0;
+    int* tile_ptr = nullptr;
+    int* tile_col = nullptr;
+    int* tile_eptr = nullptr;
+    uint32_t* ents = nullptr;
 };
 
 namespace vcsrmc {
@@ -101,6 +112,10 @@ void free_device(vcsrmc_device_format* d) {
     cudaFree(d->cols);
     cudaFree(d->rvals);
     cudaFree(d->split_rows);
+    cudaFree(d->tile_ptr);
+    cudaFree(d->tile_col);
+    cudaFree(d->tile_eptr);
+    cudaFree(d->ents);
     if (prev >= 0) cudaSetDevice(prev);
     delete d;
 }
@@ -170,12 +185,15 @@ void check_spmm_args(const vcsrmc_device_format* d, const void* B, int b_dtype, 
 }
 
 int resolve_plan(const vcsrmc_device_format* d, int plan) {
-    if (plan == VCSRMC_PLAN_AUTO) plan = d->has_rows ? VCSRMC_PLAN_ROWS : VCSRMC_PLAN_SEGMENT;
+    if (plan == VCSRMC_PLAN_AUTO)
+        plan = d->has_band ? VCSRMC_PLAN_BAND : d->has_rows ? VCSRMC_PLAN_ROWS : VCSRMC_PLAN_SEGMENT;
     if (plan == VCSRMC_PLAN_ROWS && !d->has_rows)
         throw StatusError(VCSRMC_INVALID_ARG, "the ROWS plan layout was not uploaded");
     if (plan == VCSRMC_PLAN_SEGMENT && !d->has_segment)
         throw StatusError(VCSRMC_INVALID_ARG, "the SEGMENT plan layout was not uploaded");
-    if (plan != VCSRMC_PLAN_ROWS && plan != VCSRMC_PLAN_SEGMENT)
+    if (plan == VCSRMC_PLAN_BAND && !d->has_band)
+        throw StatusError(VCSRMC_INVALID_ARG, "the BAND plan layout was not uploaded");
+    if (plan != VCSRMC_PLAN_ROWS && plan != VCSRMC_PLAN_SEGMENT && plan != VCSRMC_PLAN_BAND)
         throw StatusError(VCSRMC_INVALID_ARG, "unknown plan");
     return plan;
 }
@@ -198,6 +216,21 @@ void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int6
         P.scale = d->scale;
         e = dev::spmm_rows(P, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, C, ldc, accumulate != 0, st);
         cuda_check(e, "SpMM launch (rows plan)");
+        return;
+    }
+    if (plan == VCSRMC_PLAN_BAND) {
+        dev::BandPlanView P;
+        P.tile_ptr = d->tile_ptr;
+        P.tile_col = d->tile_col;
+        P.tile_eptr = d->tile_eptr;
+        P.ents = d->ents;
+        P.n_bands = d->n_bands;
+        P.M = d->M;
+        P.N = d->N;
+        P.scale = d->scale;
+        P.status = d->status;
+        e = dev::spmm_band(P, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, C, ldc, accumulate != 0, st);
+        cuda_check(e, "SpMM launch (band plan)");
         return;
     }
     if (!accumulate && d->M > 0) {
@@ -246,13 +279,21 @@ cudaError_t gen_dense_device(int64_t rows, int cols, uint64_t seed, int f16, voi
 
 using namespace vcsrmc;
 
-VCSRMC_EXPORT int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans, void* stream,
-                                   vcsrmc_device_format** out) {
+VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const vcsrmc_upload_options* opts,
+                                     void* stream, vcsrmc_device_format** out) {
     return guarded([&] {
-        if (!f || !out) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        if (!f || !out || !opts) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        for (int r : opts->reserved)
+            if (r != 0) throw StatusError(VCSRMC_INVALID_ARG, "reserved upload options must be 0");
+        int plans = opts->plans;
         if (plans == 0) plans = (1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS);
-        if (plans & ~((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS)))
+        if (plans & ~((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS) | (1 << VCSRMC_PLAN_BAND)))
             throw StatusError(VCSRMC_INVALID_ARG, "unknown plan bits");
+        if ((plans & (1 << VCSRMC_PLAN_BAND)) && f->v.fp32)
+            throw StatusError(VCSRMC_INVALID_ARG, "the BAND plan runs on the tensor cores and needs the FP16 format");
+        int unit_nnz = opts->rows_unit_nnz;
+        if (unit_nnz != 0 && (unit_nnz < 16 || unit_nnz > dev::kUnitNnzMax || (unit_nnz & (unit_nnz - 1))))
+            throw StatusError(VCSRMC_INVALID_ARG, "rows_unit_nnz must be 0 or a power of two in [16, 1024]");
         const VCSRMC& v = f->v;
         validate_format(v);
         if (device < 0) cuda_check(cudaGetDevice(&device), "cudaGetDevice");
@@ -297,8 +338,28 @@ VCSRMC_EXPORT int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans
                 }
                 d->has_segment = true;
             }
+            dev::RowViewHost rv;
+            if (plans & ((1 << VCSRMC_PLAN_ROWS) | (1 << VCSRMC_PLAN_BAND))) {
+                if (unit_nnz == 0) {
+                    int sms = 0;
+                    cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
+                    const int64_t nnz = std::count_if(v.lcol.begin(), v.lcol.end(), [](int c) { return c >= 0; });
+                    unit_nnz = dev::choose_unit_nnz(nnz, sms);
+                }
+                rv = dev::build_row_view(v, unit_nnz);
+                if (plans & (1 << VCSRMC_PLAN_BAND)) {
+                    dev::BandViewHost bv = dev::build_band_view(rv, v.M, nth);
+                    d->n_bands = int(bv.tile_ptr.size()) - 1;
+                    d->n_tiles = int64_t(bv.tile_col.size());
+                    d->tile_ptr = upload_array(bv.tile_ptr.data(), bv.tile_ptr.size(), st);
+                    d->tile_col = upload_array(bv.tile_col.data(), bv.tile_col.size(), st);
+                    d->tile_eptr = upload_array(bv.tile_eptr.data(), bv.tile_eptr.size(), st);
+                    d->ents = upload_array(bv.ents.data(), bv.ents.size(), st);
+                    cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+                    d->has_band = true;
+                }
+            }
             if (plans & (1 << VCSRMC_PLAN_ROWS)) {
-                dev::RowViewHost rv = dev::build_row_view(v);
                 d->rp = upload_array(rv.rp.data(), rv.rp.size(), st);
                 d->cols = upload_array(rv.cols.data(), rv.cols.size(), st);
                 static_assert(sizeof(dev::RowViewHost::Unit) == sizeof(int4), "unit layout");
@@ -327,6 +388,13 @@ VCSRMC_EXPORT int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans
         }
         *out = d;
     });
+}
+
+VCSRMC_EXPORT int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans, void* stream,
+                                   vcsrmc_device_format** out) {
+    vcsrmc_upload_options o{};
+    o.plans = plans;
+    return vcsrmc_upload_opts(f, device, &o, stream, out);
 }
 
 VCSRMC_EXPORT int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out) {

@@ -1,0 +1,45 @@
+// Row-band SpMM plan on the tensor cores (FP16 format): C written once per band of rows.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "plan_rows.hpp"
+
+namespace vcsrmc {
+namespace dev {
+
+constexpr int kBandRows = 128;  // rows per band = tcgen05 tile M
+constexpr int kBandK = 32;      // columns of A (= rows of B) per tile: two K = 16 MMA steps
+
+// Host-side band view. Band b covers rows [128 b, 128 b + 128). Its tiles are
+// [tile_ptr[b], tile_ptr[b+1]) in ascending column order; tile t covers columns
+// [tile_col[t], tile_col[t] + 32) and holds entries [tile_eptr[t], tile_eptr[t+1]).
+// An entry packs the local column (bits 0-4), the row within the band (bits 5-11) and the
+// fp16 value (bits 16-31).
+struct BandViewHost {
+    std::vector<int> tile_ptr, tile_col, tile_eptr;
+    std::vector<uint32_t> ents;
+};
+
+// From the row view (rows' entries in ascending column order, values already divided by the
+// format's scale). nthreads <= 0: all host threads.
+BandViewHost build_band_view(const RowViewHost& rv, int M, int nthreads);
+
+struct BandPlanView {
+    const int* tile_ptr;
+    const int* tile_col;
+    const int* tile_eptr;
+    const uint32_t* ents;
+    int n_bands;
+    int M, N;
+    float scale;
+    uint32_t* status;
+};
+
+cudaError_t spmm_band(const BandPlanView& P, const void* B, int b_is_f16, int64_t ldb, int O, float* C, int64_t ldc,
+                      bool accumulate, cudaStream_t st);
+
+}  // namespace dev
+}  // namespace vcsrmc

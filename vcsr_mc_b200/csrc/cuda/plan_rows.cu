@@ -7,8 +7,10 @@
 // 12 GB job. This plan consumes the same VCSR-MC data transposed at upload time into a row
 // view: row r's entries are its (group, lane) slots over all groups in format order, i.e. in
 // ascending segment and local column. A lane group owns a unit of work:
-//   * a run of up to kUnitRows consecutive light rows with together <= kUnitNnz entries, or
-//   * one kUnitNnz-entry chunk of a heavy row (more than kUnitNnz entries);
+//   * a run of up to kUnitRows consecutive light rows with together <= unit_nnz entries, or
+//   * one unit_nnz-entry chunk of a heavy row (more than unit_nnz entries);
+// unit_nnz (16 .. 1024) is chosen per matrix at upload: small matrices get small units so that
+// every SM has enough lane groups in flight.
 // each lane gathers 16 bytes of every entry's B row (fp16 B: 16 lanes cover one 256-byte row,
 // so a warp runs two units; fp32 B: 32 lanes), accumulates in fp32 registers, and stores a C
 // row once, at its last entry (16-byte streaming stores); a heavy-row chunk adds its partial
@@ -306,7 +308,14 @@ cudaError_t spmm_rows(const RowPlanView& P, const void* B, int b_is_f16, int64_t
 }
 
 // ---- host: the row view of a VCSR-MC format ------------------------------------------------------
-RowViewHost build_row_view(const VCSRMC& v) {
+int choose_unit_nnz(int64_t nnz, int sms) {
+    const int64_t target_units = int64_t(std::max(sms, 1)) * 48 * 4;
+    int u = 256;
+    while (u > 16 && nnz / u < target_units) u >>= 1;
+    return u;
+}
+
+RowViewHost build_row_view(const VCSRMC& v, int unit_nnz) {
     RowViewHost h;
     const int M = v.M;
     const int64_t G = int64_t(v.group_depth.size());
@@ -347,20 +356,20 @@ RowViewHost build_row_view(const VCSRMC& v) {
     // work units: heavy-row chunks first, then runs of light rows
     for (int r = 0; r < M; ++r) {
         const int len = h.rp[r + 1] - h.rp[r];
-        if (len > kUnitNnz) {
+        if (len > unit_nnz) {
             h.split_rows.push_back(r);
-            for (int p = h.rp[r]; p < h.rp[r + 1]; p += kUnitNnz)
-                h.units.push_back({r, int((unsigned(r + 1)) | 0x80000000u), p, std::min(h.rp[r + 1], p + kUnitNnz)});
+            for (int p = h.rp[r]; p < h.rp[r + 1]; p += unit_nnz)
+                h.units.push_back({r, int((unsigned(r + 1)) | 0x80000000u), p, std::min(h.rp[r + 1], p + unit_nnz)});
         }
     }
     int r = 0;
     while (r < M) {
-        if (h.rp[r + 1] - h.rp[r] > kUnitNnz) { ++r; continue; }
+        if (h.rp[r + 1] - h.rp[r] > unit_nnz) { ++r; continue; }
         const int rb = r;
         int n = 0;
         while (r < M && r - rb < kUnitRows) {
             const int len = h.rp[r + 1] - h.rp[r];
-            if (len > kUnitNnz || (r > rb && n + len > kUnitNnz)) break;
+            if (len > unit_nnz || (r > rb && n + len > unit_nnz)) break;
             n += len;
             ++r;
         }

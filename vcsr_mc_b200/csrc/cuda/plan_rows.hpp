@@ -10,7 +10,7 @@
 namespace vcsrmc {
 namespace dev {
 
-constexpr int kUnitNnz = 256;  // entries per warp unit (heavier rows are split into chunks)
+constexpr int kUnitNnzMax = 1024;  // entries per work unit: a power of two in [16, kUnitNnzMax]
 constexpr int kUnitRows = 16;  // light rows per unit at most (one row end per lane of a 16-lane group)
 
 // Host-side row view: row r's entries are cols/vals[rp[r], rp[r+1]) in ascending column order;
@@ -23,7 +23,11 @@ struct RowViewHost {
     std::vector<int> split_rows;
 };
 
-RowViewHost build_row_view(const VCSRMC& v);
+// unit_nnz: entries per work unit (rows with more are split into chunks of unit_nnz).
+RowViewHost build_row_view(const VCSRMC& v, int unit_nnz);
+// The unit size for a matrix of `nnz` entries on a GPU with `sms` SMs: the largest power of two
+// in [16, 256] that still gives every resident lane group (48 per SM) about four units.
+int choose_unit_nnz(int64_t nnz, int sms);
 
 struct RowPlanView {
     const int4* units;

@@ -20,13 +20,12 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
-#include <cudaTypedefs.h>
 
 #include <cstring>
-#include <mutex>
 
 #include "common.cuh"
 #include "spmm_launch.hpp"
+#include "tma_host.hpp"
 
 namespace vcsrmc {
 namespace dev {
@@ -224,19 +223,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
 template <int TKI, int SW, bool kTma, typename BT>
 cudaError_t launch_tc(const DeviceFormatView& F, const CUtensorMap& tmap, const BT* B, int64_t ldb, int O, float* C,
                       int64_t ldc, cudaStream_t st) {
@@ -254,26 +240,13 @@ template <int TKI, int SW>
 cudaError_t dispatch_b(const DeviceFormatView& F, const void* B, int b_is_f16, int64_t ldb, int O, float* C,
                        int64_t ldc, cudaStream_t st) {
     CUtensorMap tmap;
-    std::memset(&tmap, 0, sizeof(tmap));
     if (b_is_f16) {
         const __half* Bh = static_cast<const __half*>(B);
-        // TMA needs a 16-byte aligned base, a row pitch that is a multiple of 16 bytes, and
-        // (kept simple here) at least one full box of columns and rows.
-        const bool tma_ok = (reinterpret_cast<uintptr_t>(B) & 15) == 0 && ((ldb * 2) & 15) == 0 && ldb >= O &&
-                            O >= 64 && F.N >= SW;
-        PFN_cuTensorMapEncodeTiled_v12000 enc = tma_ok ? tensor_map_encoder() : nullptr;
-        if (enc) {
-            const cuuint64_t dims[2] = {cuuint64_t(O), cuuint64_t(F.N)};
-            const cuuint64_t strides[1] = {cuuint64_t(ldb) * 2};
-            const cuuint32_t box[2] = {64u, cuuint32_t(SW)};
-            const cuuint32_t estr[2] = {1u, 1u};
-            const CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(B), dims, strides,
-                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-            if (r == CUDA_SUCCESS) return launch_tc<TKI, SW, true, __half>(F, tmap, Bh, ldb, O, C, ldc, st);
-        }
+        if (encode_b_tmap_f16(&tmap, B, ldb, O, F.N, SW))
+            return launch_tc<TKI, SW, true, __half>(F, tmap, Bh, ldb, O, C, ldc, st);
         return launch_tc<TKI, SW, false, __half>(F, tmap, Bh, ldb, O, C, ldc, st);
     }
+    std::memset(&tmap, 0, sizeof(tmap));
     return launch_tc<TKI, SW, false, float>(F, tmap, static_cast<const float*>(B), ldb, O, C, ldc, st);
 }
 

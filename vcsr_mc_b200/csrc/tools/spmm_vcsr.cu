@@ -2,7 +2,7 @@
 //   --mtx FILE | --gen c1|c2|c3|rmat[:scale]  --O 128 --segw 16 --tileK 64 --repeat 10 --warmup 3
 //   --stat mean|median --reorder none|rcm --algo vcsr_mc,vcsr_mc_fp32,cusparse,cusparse_fp16|all
 //   --check cpu|none --csv --bdist pattern|normal|uniform|wide --lenient
-// plus: --gen (seeded synthetic configurations, no download needed), --seed, --plan auto|rows|segment,
+// plus: --gen (seeded synthetic configurations, no download needed), --seed, --plan auto|rows|segment|band,
 // --b16 (the FP16 path reads fp16 B instead of converting fp32 B).
 // Same B fill (fixed seed 20260923), same fp64 CPU check and acceptance bounds, same CSV schema.
 // Host work uses the library's C++ surface (vcsrmc/*.hpp); every GPU call goes through the C ABI
@@ -60,7 +60,7 @@ void usage() {
         "            cusparse_fp16 (FP16 A and B, FP32 compute and C), all\n"
         "Options: --segw 16 --tileK 64 --repeat 10 --warmup 3 --stat mean|median\n"
         "         --reorder none|rcm --check cpu|none --csv --bdist pattern|normal|uniform|wide\n"
-        "         --lenient --seed 0 --plan auto|rows|segment --b16\n"
+        "         --lenient --seed 0 --plan auto|rows|segment|band --b16\n"
         "tileK must be one of 16, 32, 64, 128, 256; segw one of 16, 32, 48, 64.\n");
 }
 
@@ -171,8 +171,12 @@ static int benchmark_main(int argc, char** argv) {
     if ((mtx.empty() == gen.empty()) || optind != argc) { usage(); return 2; }
     if (reorder != "none" && reorder != "rcm") throw std::runtime_error("Unknown reordering: " + reorder);
     if (stat != "mean" && stat != "median") throw std::runtime_error("Unknown --stat: " + stat + " (mean|median)");
-    if (plan != "auto" && plan != "rows" && plan != "segment") throw std::runtime_error("Unknown --plan: " + plan);
-    const int plan_id = plan == "rows" ? VCSRMC_PLAN_ROWS : plan == "segment" ? VCSRMC_PLAN_SEGMENT : VCSRMC_PLAN_AUTO;
+    if (plan != "auto" && plan != "rows" && plan != "segment" && plan != "band")
+        throw std::runtime_error("Unknown --plan: " + plan);
+    const int plan_id = plan == "rows"      ? VCSRMC_PLAN_ROWS
+                        : plan == "segment" ? VCSRMC_PLAN_SEGMENT
+                        : plan == "band"    ? VCSRMC_PLAN_BAND
+                                            : VCSRMC_PLAN_AUTO;
 
     CSR csr = mtx.empty() ? generate(gen, seed) : coo_to_csr(read_matrix_market_coo(mtx));
     const std::string source = mtx.empty() ? "gen:" + gen : mtx;
@@ -310,7 +314,11 @@ static int benchmark_main(int argc, char** argv) {
             vcsrmc_device_format* hd = nullptr;
             abi_ok(vcsrmc_csr_from_arrays(csr.M, csr.N, csr.nnz, csr.row_ptr.data(), csr.col.data(), csr.val.data(), &hc));
             abi_ok(vcsrmc_build_host(hc, fp32 ? 1 : 0, segw, 0, &hf));
-            const float upload = wall_ms([&] { abi_ok(vcsrmc_upload(hf, device_id, st, &hd)); });
+            // the BAND plan runs on the tensor cores (FP16 format); the FP32 format takes ROWS
+            const int my_plan = (plan_id == VCSRMC_PLAN_BAND && fp32) ? VCSRMC_PLAN_ROWS : plan_id;
+            const int mask = my_plan == VCSRMC_PLAN_BAND ? (1 << VCSRMC_PLAN_BAND) : 0;
+            const char* my_plan_name = my_plan == plan_id ? plan.c_str() : "rows";
+            const float upload = wall_ms([&] { abi_ok(vcsrmc_upload_ex(hf, device_id, mask, st, &hd)); });
             measure(name,
                     [&] {
                         cudaEvent_t a, b;
@@ -318,7 +326,7 @@ static int benchmark_main(int argc, char** argv) {
                         cudaEventCreate(&b);
                         cudaEventRecord(a, st);
                         abi_ok(vcsrmc_spmm_ex(hd, use_b16 ? static_cast<const void*>(dB16) : dB,
-                                              use_b16 ? VCSRMC_F16 : VCSRMC_F32, O, O, tileK, dC, O, 1, plan_id, st));
+                                              use_b16 ? VCSRMC_F16 : VCSRMC_F32, O, O, tileK, dC, O, 1, my_plan, st));
                         cudaEventRecord(b, st);
                         cudaEventSynchronize(b);
                         float ms = 0;
@@ -327,7 +335,7 @@ static int benchmark_main(int argc, char** argv) {
                         cudaEventDestroy(b);
                         return ms;
                     },
-                    convert + upload, convert, upload, plan.c_str());
+                    convert + upload, convert, upload, my_plan_name);
             vcsrmc_device_free(hd);
             vcsrmc_format_free(hf);
             vcsrmc_csr_free(hc);
