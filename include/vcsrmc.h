@@ -50,7 +50,7 @@ extern "C" {
  * BAND:    FP16 format only: bands of 128 rows, tiles of 32 columns multiplied on the tensor
  *          cores into one accumulator per band, C stored once. For matrices whose rows touch
  *          few column windows (stencils, banded or reordered matrices).
- * AUTO:    BAND, ROWS, SEGMENT: the first whose layout is resident.                        */
+ * AUTO:    the first resident layout of BAND (fp16 B only), ROWS, SEGMENT, BAND.          */
 #define VCSRMC_PLAN_AUTO 0
 #define VCSRMC_PLAN_SEGMENT 1
 #define VCSRMC_PLAN_ROWS 2
@@ -135,8 +135,9 @@ void vcsrmc_format_free(vcsrmc_format* f);
  * the device). Blocking. */
 int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out);
 /* Same, choosing which plan layouts to make resident: a bit mask of (1 << VCSRMC_PLAN_SEGMENT),
- * (1 << VCSRMC_PLAN_ROWS) and (1 << VCSRMC_PLAN_BAND); 0 = SEGMENT and ROWS (what vcsrmc_upload
- * does). */
+ * (1 << VCSRMC_PLAN_ROWS) and (1 << VCSRMC_PLAN_BAND). 0 (what vcsrmc_upload does) = SEGMENT and
+ * ROWS, plus BAND for an FP16 format whose 128-row x 32-column tiles hold enough entries to
+ * beat ROWS (estimated from a sample of bands). */
 int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans, void* stream,
                      vcsrmc_device_format** out);
 /* Upload tuning; zero-initialise and set what you need (0 = the library's choice). */
@@ -145,7 +146,8 @@ typedef struct {
     int32_t rows_unit_nnz; /* ROWS plan: entries per work unit, a power of two in [16, 1024];
                               rows with more entries are split into chunks of this size.
                               0 = chosen from the matrix so that every SM gets enough units.  */
-    int32_t reserved[6];   /* must be 0                                                        */
+    int32_t band_rows;     /* BAND plan: rows per band, 1 .. 128; 0 = chosen from the matrix    */
+    int32_t reserved[5];   /* must be 0                                                        */
 } vcsrmc_upload_options;
 int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const vcsrmc_upload_options* opts,
                        void* stream, vcsrmc_device_format** out);

@@ -21,13 +21,13 @@ PLAN_IDS = ["segment", "rows", "band"]
 
 def run_gpu(torch, A: vm.CSR, B32: np.ndarray, fp32: bool, segw: int, tileK: int, b_half: bool,
             accumulate_into=None, ldb_pad: int = 0, ldc_pad: int = 0, plan: int = vm.PLAN_SEGMENT,
-            unit_nnz: int = 0):
+            unit_nnz: int = 0, band_rows: int = 0):
     """C = A*B (or C = accumulate_into + A*B) on cuda:0 with one plan; returns (C, B values used)."""
     if plan == vm.PLAN_BAND and fp32:
         pytest.skip("the BAND plan runs on the tensor cores: FP16 format only")
     O = B32.shape[1]
     V = vm.csr_to_vcsr_mc(A, fp32=fp32, segw=segw)
-    dV = vm.upload_vcsr_mc_device(V, device=0, plans=[plan], rows_unit_nnz=unit_nnz)
+    dV = vm.upload_vcsr_mc_device(V, device=0, plans=[plan], rows_unit_nnz=unit_nnz, band_rows=band_rows)
     dt = torch.float16 if b_half else torch.float32
     Bfull = torch.zeros((B32.shape[0], O + ldb_pad), dtype=dt, device="cuda")
     Bfull[:, :O] = torch.from_numpy(B32).to(device="cuda", dtype=dt)
@@ -223,6 +223,28 @@ def test_band_plan_shapes(cuda, n):
     rp, col, val = random_csr(n, n, min(1.0, 6.0 / n), seed=n, empty_rows=True)
     A = vm.CSR.from_arrays(n, n, rp, col, val)
     B = np.random.default_rng(n).uniform(-1, 1, size=(n, 128)).astype(np.float32)
+    C, Bu = run_gpu(cuda, A, B, False, 32, 128, b_half=True, plan=vm.PLAN_BAND)
+    oracle_check(A, C, Bu, False)
+
+
+@pytest.mark.parametrize("band_rows", [1, 37, 64, 126, 128])
+@pytest.mark.parametrize("accumulate", [False, True], ids=["store", "accumulate"])
+def test_band_plan_heights(cuda, band_rows, accumulate):
+    """BAND plan at fixed band heights: tiles start at any column (greedy), rows past a band's
+    height are never stored, C += A*B adds."""
+    A = vm.CSR.generate(vm.GEN_STENCIL27, 12, seed=0)
+    B = vm.gen_dense_host(A.N, 128, seed=3)
+    base = np.random.default_rng(4).uniform(-1, 1, size=(A.M, 128)).astype(np.float32) if accumulate else None
+    C, Bu = run_gpu(cuda, A, B, False, 32, 128, b_half=True, accumulate_into=base, plan=vm.PLAN_BAND,
+                    band_rows=band_rows)
+    oracle_check(A, C, Bu, False, base=None if base is None else base.astype(np.float64))
+
+
+def test_band_plan_dense_tiles(cuda):
+    """Tiles with more entries than the producers keep in registers (whole-tile clears)."""
+    rp, col, val = random_csr(256, 96, 0.9, seed=8)
+    A = vm.CSR.from_arrays(256, 96, rp, col, val)
+    B = np.random.default_rng(8).uniform(-1, 1, size=(96, 200)).astype(np.float32)
     C, Bu = run_gpu(cuda, A, B, False, 32, 128, b_half=True, plan=vm.PLAN_BAND)
     oracle_check(A, C, Bu, False)
 

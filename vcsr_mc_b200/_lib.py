@@ -33,7 +33,8 @@ class VcsrmcError(RuntimeError):
 
 
 class UploadOptions(ctypes.Structure):
-    _fields_ = [("plans", ctypes.c_int32), ("rows_unit_nnz", ctypes.c_int32), ("reserved", ctypes.c_int32 * 6)]
+    _fields_ = [("plans", ctypes.c_int32), ("rows_unit_nnz", ctypes.c_int32), ("band_rows", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 5)]
 
 
 class CsrView(ctypes.Structure):

@@ -214,13 +214,15 @@ class DeviceVCSRMC:
 
 
 def upload_vcsr_mc_device(V: VCSRMC, device: int = 0, stream=None, plans=None,
-                          rows_unit_nnz: int = 0) -> DeviceVCSRMC:
+                          rows_unit_nnz: int = 0, band_rows: int = 0) -> DeviceVCSRMC:
     """Copies the format to `device`. plans: iterable of PLAN_SEGMENT / PLAN_ROWS / PLAN_BAND
-    layouts to make resident (default: SEGMENT and ROWS; BAND needs the FP16 format). rows_unit_nnz: entries per ROWS-plan work unit (0 = the library's
-    choice for this matrix)."""
+    layouts to make resident (default: SEGMENT and ROWS, plus BAND for FP16 formats whose
+    column tiles are dense enough; BAND needs the FP16 format). rows_unit_nnz: entries per ROWS-plan work unit (0 = the library's
+    choice for this matrix). band_rows: rows per BAND-plan band, 1 .. 128 (0 = chosen)."""
     opts = _lib.UploadOptions()
     opts.plans = 0 if plans is None else sum(1 << p for p in set(plans))
     opts.rows_unit_nnz = rows_unit_nnz
+    opts.band_rows = band_rows
     h = ctypes.c_void_p()
     call("vcsrmc_upload_opts", V.handle, device, ctypes.byref(opts), _stream_handle(stream), ctypes.byref(h))
     return DeviceVCSRMC(h, V, device)

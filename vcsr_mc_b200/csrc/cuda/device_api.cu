@@ -52,7 +52,7 @@ struct vcsrmc_device_format {
     int n_split_rows = 0;
     // BAND plan
     bool has_band = false;
-    int n_bands = 0;
+    int n_bands = 0, band_rows = 0;
     int64_t n_tiles = 0;
     int* tile_ptr = nullptr;
     int* tile_col = nullptr;
@@ -184,9 +184,15 @@ void check_spmm_args(const vcsrmc_device_format* d, const void* B, int b_dtype, 
     if ((d->N > 0 && !B) || (d->M > 0 && !C)) throw StatusError(VCSRMC_INVALID_ARG, "NULL B or C");
 }
 
-int resolve_plan(const vcsrmc_device_format* d, int plan) {
-    if (plan == VCSRMC_PLAN_AUTO)
-        plan = d->has_band ? VCSRMC_PLAN_BAND : d->has_rows ? VCSRMC_PLAN_ROWS : VCSRMC_PLAN_SEGMENT;
+// AUTO: BAND for fp16 B (its tiles are TMA copies of fp16 B; fp32 B would be converted tile by
+// tile), then ROWS, then SEGMENT, then BAND for fp32 B; the first whose layout is resident.
+int resolve_plan(const vcsrmc_device_format* d, int plan, int b_dtype) {
+    if (plan == VCSRMC_PLAN_AUTO) {
+        if (d->has_band && b_dtype == VCSRMC_F16) plan = VCSRMC_PLAN_BAND;
+        else if (d->has_rows) plan = VCSRMC_PLAN_ROWS;
+        else if (d->has_segment) plan = VCSRMC_PLAN_SEGMENT;
+        else plan = VCSRMC_PLAN_BAND;
+    }
     if (plan == VCSRMC_PLAN_ROWS && !d->has_rows)
         throw StatusError(VCSRMC_INVALID_ARG, "the ROWS plan layout was not uploaded");
     if (plan == VCSRMC_PLAN_SEGMENT && !d->has_segment)
@@ -200,7 +206,7 @@ int resolve_plan(const vcsrmc_device_format* d, int plan) {
 
 void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int64_t ldb, int32_t O, int32_t tileK,
                  float* C, int64_t ldc, int accumulate, int plan, cudaStream_t st) {
-    plan = resolve_plan(d, plan);
+    plan = resolve_plan(d, plan, b_dtype);
     cudaError_t e;
     if (plan == VCSRMC_PLAN_ROWS) {
         dev::RowPlanView P;
@@ -225,6 +231,7 @@ void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int6
         P.tile_eptr = d->tile_eptr;
         P.ents = d->ents;
         P.n_bands = d->n_bands;
+        P.band_rows = d->band_rows;
         P.M = d->M;
         P.N = d->N;
         P.scale = d->scale;
@@ -286,7 +293,8 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
         for (int r : opts->reserved)
             if (r != 0) throw StatusError(VCSRMC_INVALID_ARG, "reserved upload options must be 0");
         int plans = opts->plans;
-        if (plans == 0) plans = (1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS);
+        const bool default_plans = plans == 0;
+        if (default_plans) plans = (1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS);
         if (plans & ~((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS) | (1 << VCSRMC_PLAN_BAND)))
             throw StatusError(VCSRMC_INVALID_ARG, "unknown plan bits");
         if ((plans & (1 << VCSRMC_PLAN_BAND)) && f->v.fp32)
@@ -294,6 +302,8 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
         int unit_nnz = opts->rows_unit_nnz;
         if (unit_nnz != 0 && (unit_nnz < 16 || unit_nnz > dev::kUnitNnzMax || (unit_nnz & (unit_nnz - 1))))
             throw StatusError(VCSRMC_INVALID_ARG, "rows_unit_nnz must be 0 or a power of two in [16, 1024]");
+        if (opts->band_rows < 0 || opts->band_rows > dev::kBandRows)
+            throw StatusError(VCSRMC_INVALID_ARG, "band_rows must be 0 or in [1, 128]");
         const VCSRMC& v = f->v;
         validate_format(v);
         if (device < 0) cuda_check(cudaGetDevice(&device), "cudaGetDevice");
@@ -347,8 +357,16 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
                     unit_nnz = dev::choose_unit_nnz(nnz, sms);
                 }
                 rv = dev::build_row_view(v, unit_nnz);
+                // The default layouts add the BAND plan (FP16 format) where it beats ROWS:
+                // enough entries per tensor-core tile.
+                dev::BandChoice bc{dev::kBandRows, 0.0};
+                if ((plans & (1 << VCSRMC_PLAN_BAND)) || (default_plans && !v.fp32)) bc = dev::choose_band(rv, v.M);
+                if (opts->band_rows > 0) bc.band_rows = opts->band_rows;
+                if (default_plans && !v.fp32 && bc.entries_per_tile >= dev::kBandMinEntriesPerTile)
+                    plans |= 1 << VCSRMC_PLAN_BAND;
                 if (plans & (1 << VCSRMC_PLAN_BAND)) {
-                    dev::BandViewHost bv = dev::build_band_view(rv, v.M, nth);
+                    dev::BandViewHost bv = dev::build_band_view(rv, v.M, bc.band_rows, nth);
+                    d->band_rows = bv.band_rows;
                     d->n_bands = int(bv.tile_ptr.size()) - 1;
                     d->n_tiles = int64_t(bv.tile_col.size());
                     d->tile_ptr = upload_array(bv.tile_ptr.data(), bv.tile_ptr.size(), st);

@@ -1,28 +1,30 @@
-// Row-band execution plan for the FP16 format on the 5th-generation tensor cores: every CTA
-// owns a band of 128 consecutive rows of A and a 128-column slab of B and C, accumulates the
-// band's product over its column tiles in tensor memory, and writes its C tile once.
+// Row-band execution plan for the FP16 format on the 5th-generation tensor cores: each band of
+// up to 128 consecutive rows of A, times a 128-column slab of B, is accumulated over its column
+// tiles in tensor memory and its C tile is written once.
 //
 // The reference's FP16 dataflow (src/vcsr_mc.cu:143-237) multiplies densified 16-row groups of
 // one segment by that segment's rows of B and adds every group into C with atomics. Here the
 // same tcgen05 tile product (A densified from (column, value) entries in shared memory, B staged
 // by TMA with the 128-byte swizzle, fp32 accumulation) runs row-stationary:
-//   * a tile = the band's entries in 32 consecutive columns; tiles of a band are visited in
-//     ascending column order, each adding a 128 x 32 by 32 x 128 product into one TMEM
-//     accumulator (M = 128, N = 128, two K = 16 steps);
-//   * 4 shared-memory stages of (B 8 KB, A 8 KB) and 5 warps: producer warp w owns stage w and
-//     the tiles w, w + 4, ...: once the MMAs of its previous tile have completed it starts the
-//     TMA load of the next B tile, clears its previous entries from the A tile (the positions
-//     it remembers, or the whole tile after a large one), writes the new entries and arrives on
-//     the stage's barrier; lane 0 of the fifth warp issues the MMAs in tile order. Producers
-//     load their next tile's entries and bounds before they wait, so four tiles are being
-//     prepared while the tensor cores work;
-//   * epilogue: tcgen05.ld (warp w: rows 32w .. 32w+31), scale, one streaming store per C
-//     element; C is never read (or read once, for C += A*B).
+//   * a tile = a band's entries in 32 consecutive columns starting at the first column not
+//     covered by the previous tile; each adds a (band x 32) by (32 x 128) product into the
+//     band's TMEM accumulator (M = 128, N = 128, two K = 16 steps);
+//   * persistent CTAs (two per SM) walk their work items (band, slab) in a strided order; the
+//     tiles of all their items form one sequence through 5 shared-memory stages (B 8 KB, A
+//     8 KB). Producer warp w owns stage w: once the MMAs of its previous tile have completed it
+//     starts the TMA load of its next B tile, prefetches the one after into L2, clears its
+//     previous entries from the A tile (the positions it remembers, or the whole tile after a
+//     large one), writes the new entries and arrives on the stage's barrier. Its registers run
+//     one position ahead (entries and bounds are loaded two iterations before use);
+//   * lane 0 of the MMA warp issues the MMAs in sequence order into one of two TMEM
+//     accumulators (256 columns), so the MMAs of a band overlap the epilogue of the previous one;
+//   * four epilogue warps read their TMEM lane quarter (tcgen05.ld), transpose 32 x 32 blocks
+//     through shared memory and write C with whole 128-byte lines (read once for C += A*B).
 // B traffic per band is the B rows of its tiles (32 x 256 bytes each), which neighbouring bands
 // share in L2; this suits matrices whose rows touch few column windows (stencils, banded or
 // reordered matrices). Matrices with scattered columns are served better by the ROWS plan.
-// Every wait is bounded; on expiry the kernel drains what it issued, flags the format's status
-// word, frees its tensor memory and exits.
+// Every wait is bounded; on expiry the CTA's warps stop, drain what they issued, the format's
+// status word is flagged and the tensor memory is freed.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -41,20 +43,30 @@ namespace vcsrmc {
 namespace dev {
 namespace {
 
-constexpr int kSlab = 128;                       // columns of B and C per CTA = MMA N
-constexpr int kStages = 4;
-constexpr int kProducers = kStages;              // producer warp w fills stage w: tiles i = w mod kStages
-constexpr int kMmaWarp = kProducers;             // + one warp whose lane 0 issues the MMAs
-constexpr int kThreads = (kProducers + 1) * 32;
-constexpr int kSaved = 4;                        // entries a producer lane keeps per tile (to clear them)
+constexpr int kSlab = 128;                       // columns of B and C per work item = MMA N
+constexpr int kStages = 5;
+constexpr int kProducers = kStages;              // warps 0-4: producer w fills stage w
+constexpr int kMmaWarp = kProducers;             // warp 5: lane 0 issues the MMAs
+constexpr int kEpiWarp0 = kProducers + 1;        // warps 6-9: epilogue (TMEM lane quarter = warp % 4)
+constexpr int kWarps = kEpiWarp0 + 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kCtasPerSm = 2;
+constexpr int kSaved = 8;                        // entries a producer lane keeps per tile (to clear them)
+constexpr int kAccs = 2;                         // TMEM accumulators: one band's MMAs overlap the previous epilogue
+constexpr uint32_t kTmemCols = kAccs * kSlab;
 constexpr int kPanelBytes = kBandK * 128;        // 32 rows x 64 fp16, 128-byte swizzle
 constexpr int kBBytes = 2 * kPanelBytes;
 constexpr int kABytes = kBandRows * kBandK * 2;
 constexpr int kStageBytes = kBBytes + kABytes;   // a multiple of 1024: swizzle atoms stay aligned
-constexpr int kBarOffset = kStages * kStageBytes;
-constexpr int kSmemBytes = kBarOffset + 3 * kStages * 8 + 16 + 1024;  // + barriers, slot, alignment
-constexpr uint32_t kTmemCols = kSlab;
+constexpr int kEpiStride = 36;                   // floats per row of an epilogue warp's 32 x 32 staging tile
+constexpr int kEpiBytes = 32 * kEpiStride * 4;
+constexpr int kEpiOffset = kStages * kStageBytes;
+constexpr int kBarOffset = kEpiOffset + 4 * kEpiBytes;
+constexpr int kNumBars = 3 * kStages + 2 * kAccs;
+constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // + barriers, slot, flag, alignment
 static_assert(kStageBytes % 1024 == 0, "stage alignment");
+static_assert(kCtasPerSm * kTmemCols <= 512, "tensor memory per SM");
+static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 233472, "shared memory per SM");
 
 // Byte offset of A element (row r, column c) in the K-major, unswizzled A tile: core matrices of
 // 8 rows x 16 bytes, K-adjacent ones 128 B apart (LBO), 8-row blocks kBandK * 16 B apart (SBO).
@@ -88,8 +100,84 @@ __device__ __forceinline__ void stage_b_warp(uint8_t* Bs, const BT* __restrict__
     }
 }
 
+// Bounded wait that also gives up when another warp has flagged an abort (or flags one itself
+// when its own budget runs out), so that one expired wait ends the whole CTA promptly.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag != 0) return false;
+        if (clock64() - t0 > kWaitBudgetCycles) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+// Work items of a CTA: items blockIdx.x, + gridDim.x, ...; item -> band item % n_bands and
+// column slab item / n_bands. The tiles of all its items form one sequence; position q of it
+// uses stage q % kStages.
+struct ItemRange {
+    int t_beg, nt;
+};
+__device__ __forceinline__ ItemRange item_range(const BandPlanView& P, int item, int n_items) {
+    if (item >= n_items) return ItemRange{0, 0};
+    const int b = item % P.n_bands;
+    const int t0 = __ldg(P.tile_ptr + b);
+    return ItemRange{t0, __ldg(P.tile_ptr + b + 1) - t0};
+}
+// A position in the tile sequence (the next item's range is loaded ahead).
+struct TileIter {
+    int item, t;
+    ItemRange cur, next;
+};
+__device__ __forceinline__ void iter_advance(TileIter& it, int step, const BandPlanView& P, int n_items) {
+    it.t += step;
+    while (it.item < n_items && it.t >= it.cur.nt) {
+        it.t -= it.cur.nt;
+        it.item += gridDim.x;
+        it.cur = it.next;
+        it.next = item_range(P, it.item + gridDim.x, n_items);
+    }
+}
+__device__ __forceinline__ TileIter iter_begin(const BandPlanView& P, int n_items, int step) {
+    TileIter it;
+    it.item = blockIdx.x;
+    it.t = 0;
+    it.cur = item_range(P, it.item, n_items);
+    it.next = item_range(P, it.item + gridDim.x, n_items);
+    iter_advance(it, step, P, n_items);
+    return it;
+}
+
+// A producer's registers for one position of the tile sequence.
+struct ProducerRegs {
+    TileIter it;
+    int kc, e0, e1;          // tile's first column and entry range
+    uint32_t ev[kSaved];     // its first 32 * kSaved entries, lane-strided
+};
+__device__ __forceinline__ void load_bounds(ProducerRegs& r, const BandPlanView& P, int n_items) {
+    r.kc = 0;
+    r.e0 = 0;
+    r.e1 = 0;
+    if (r.it.item < n_items) {
+        const int t = r.it.cur.t_beg + r.it.t;
+        r.kc = __ldg(P.tile_col + t);
+        r.e0 = __ldg(P.tile_eptr + t);
+        r.e1 = __ldg(P.tile_eptr + t + 1);
+    }
+}
+__device__ __forceinline__ void load_entries(ProducerRegs& r, const BandPlanView& P, int lane) {
+#pragma unroll
+    for (int k = 0; k < kSaved; ++k) {
+        const int e = r.e0 + lane + 32 * k;
+        r.ev[k] = e < r.e1 ? __ldg(P.ents + e) : 0u;
+    }
+}
+
 template <bool kTma, bool kAcc, typename BT>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     vcsr_band_kernel(BandPlanView P, const __grid_constant__ CUtensorMap tmap, const BT* __restrict__ B,
                      int64_t ldb, int O, float* __restrict__ C, int64_t ldc, int vec_c) {
     extern __shared__ uint8_t smem_raw[];
@@ -98,25 +186,13 @@ __global__ void __launch_bounds__(kThreads)
     uint64_t* full_b = reinterpret_cast<uint64_t*>(smem + kBarOffset);  // B tile of a stage landed (TMA)
     uint64_t* full_a = full_b + kStages;                                 // A tile of a stage written
     uint64_t* done = full_a + kStages;                                   // MMAs reading a stage completed
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(done + kStages);
-    int* abort_flag = reinterpret_cast<int*>(tslot + 1);
+    uint64_t* acc_full = done + kStages;                                 // a band's accumulator is complete
+    uint64_t* acc_empty = acc_full + kAccs;                              // the epilogue has read it
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + kAccs);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int band = blockIdx.x;
-    const int k0 = blockIdx.y * kSlab;
-    const int ncols = min(kSlab, O - k0);
-    const int row0 = band * kBandRows;
-    const int t_beg = P.tile_ptr[band];
-    const int nt = P.tile_ptr[band + 1] - t_beg;
-
-    if (nt == 0) {  // rows without entries (uniform across the CTA: no barrier or TMEM needed)
-        if (!kAcc)
-            for (int i = tid; i < kBandRows * ncols; i += kThreads) {
-                const int r = row0 + i / ncols;
-                if (r < P.M) C[int64_t(r) * ldc + k0 + i % ncols] = 0.f;
-            }
-        return;
-    }
+    const int n_items = P.n_bands * ((O + kSlab - 1) / kSlab);
 
     if (warp == 0) {
         tmem_alloc(tslot, kTmemCols);
@@ -126,8 +202,13 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full_b[s], 1);
-            mbar_init(&full_a[s], 32);
+            mbar_init(&full_a[s], 1);
             mbar_init(&done[s], 1);
+        }
+#pragma unroll
+        for (int a = 0; a < kAccs; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 128);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -145,53 +226,61 @@ __global__ void __launch_bounds__(kThreads)
     const uint32_t tmem = *tslot;
 
     if (warp < kProducers) {
-        // ---- producer: tiles w, w + 4, ... into stage w -------------------------------------
+        // ---- producer w: positions w, w + kStages, ... of the tile sequence, into stage w -----
         const int s = warp;
         uint8_t* Bs = smem + s * kStageBytes;
         uint8_t* As = Bs + kBBytes;
-        // The second 64-column panel of B is loaded only where it holds columns < O; past O the
-        // accumulator columns are never stored, so the panel's contents do not matter there.
-        const int npanels = k0 + 64 < O ? 2 : 1;
         int saved[kSaved];
 #pragma unroll
         for (int k = 0; k < kSaved; ++k) saved[k] = -1;
         bool prev_overflow = false;
         int last_use = -1;  // lane 0: the last use of this stage whose B load was issued
-        int kc = 0, e0 = 0, e1 = 0;
-        if (s < nt) {
-            kc = P.tile_col[t_beg + s];
-            e0 = P.tile_eptr[t_beg + s];
-            e1 = P.tile_eptr[t_beg + s + 1];
-        }
-        for (int i = s; i < nt; i += kStages) {
-            const uint32_t use = uint32_t(i / kStages);
-            // this tile's first entries and the next tile's bounds, loaded ahead of the wait
-            uint32_t ev[kSaved];
-#pragma unroll
-            for (int k = 0; k < kSaved; ++k) {
-                const int e = e0 + lane + 32 * k;
-                ev[k] = e < e1 ? __ldg(P.ents + e) : 0u;
+        uint32_t use = 0;
+        // Three register sets rotate through the roles current (bounds and first entries
+        // loaded), next (bounds loaded) and after-next; every iteration issues the loads of the
+        // next position's entries and the after-next position's bounds before it waits for its
+        // stage, and consumes them two iterations later. The loop is unrolled three times so that
+        // no register holding a pending load is ever copied (a copy would wait for the load).
+        ProducerRegs X, Y, Z;
+        X.it = iter_begin(P, n_items, s);
+        load_bounds(X, P, n_items);
+        Y.it = X.it;
+        iter_advance(Y.it, kStages, P, n_items);
+        load_bounds(Y, P, n_items);
+        load_entries(X, P, lane);
+        auto step = [&](ProducerRegs& cur, ProducerRegs& nxt, ProducerRegs& nn) -> bool {
+            if (cur.it.item >= n_items) return false;
+            load_entries(nxt, P, lane);
+            nn.it = nxt.it;
+            iter_advance(nn.it, kStages, P, n_items);
+            load_bounds(nn, P, n_items);
+            // the stage is free once the MMAs of its previous tile completed (lane 0 waits; the
+            // warp barrier orders the other lanes' writes to the stage after its observation)
+            if (use > 0) {
+                bool free = true;
+                if (lane == 0) free = wait_or_abort(&done[s], (use - 1u) & 1u, abort_flag);
+                if (!__shfl_sync(0xffffffffu, free, 0)) return false;
             }
-            int nkc = 0, ne0 = 0, ne1 = 0;
-            if (i + kStages < nt) {
-                nkc = __ldg(P.tile_col + t_beg + i + kStages);
-                ne0 = __ldg(P.tile_eptr + t_beg + i + kStages);
-                ne1 = __ldg(P.tile_eptr + t_beg + i + kStages + 1);
-            }
-            // the stage is free once the MMAs of tile i - kStages completed
-            if (use > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(&done[s], (use - 1u) & 1u))) {
-                if (lane == 0) { *abort_flag = 1; atomicOr(P.status, kStatusTimeout); }
-                break;
-            }
+            const int k0 = (cur.it.item / P.n_bands) * kSlab;
             if constexpr (kTma) {
+                // the next tile of this stage (bounds loaded an iteration ago): into L2 now, so its
+                // TMA load one iteration later does not wait for DRAM
+                if (lane == 1 && nxt.it.item < n_items) {
+                    const int nk0 = (nxt.it.item / P.n_bands) * kSlab;
+                    tma_prefetch_l2_2d(&tmap, nk0, nxt.kc);
+                    if (nk0 + 64 < O) tma_prefetch_l2_2d(&tmap, nk0 + 64, nxt.kc);
+                }
                 if (lane == 0) {
+                    // The second 64-column panel is loaded only where it holds columns < O; past O
+                    // the accumulator columns are never stored, so its contents do not matter.
+                    const int npanels = k0 + 64 < O ? 2 : 1;
                     mbar_arrive_expect_tx(&full_b[s], uint32_t(npanels * kPanelBytes));
-                    tma_load_2d(Bs, &tmap, &full_b[s], k0, kc);
-                    if (npanels == 2) tma_load_2d(Bs + kPanelBytes, &tmap, &full_b[s], k0 + 64, kc);
+                    tma_load_2d(Bs, &tmap, &full_b[s], k0, cur.kc);
+                    if (npanels == 2) tma_load_2d(Bs + kPanelBytes, &tmap, &full_b[s], k0 + 64, cur.kc);
                     last_use = int(use);
                 }
             } else {
-                stage_b_warp<BT>(Bs, B, ldb, P.N, O, kc, k0, lane);
+                stage_b_warp<BT>(Bs, B, ldb, P.N, O, cur.kc, k0, lane);
             }
             // clear the previous tile's entries: the remembered ones, or the whole tile
             if (use > 0) {
@@ -207,102 +296,160 @@ __global__ void __launch_bounds__(kThreads)
             }
 #pragma unroll
             for (int k = 0; k < kSaved; ++k) {
-                const int e = e0 + lane + 32 * k;
+                const int e = cur.e0 + lane + 32 * k;
                 saved[k] = -1;
-                if (e < e1) {
-                    saved[k] = ent_offset(ev[k]);
-                    *reinterpret_cast<uint16_t*>(As + saved[k]) = uint16_t(ev[k] >> 16);
+                if (e < cur.e1) {
+                    saved[k] = ent_offset(cur.ev[k]);
+                    *reinterpret_cast<uint16_t*>(As + saved[k]) = uint16_t(cur.ev[k] >> 16);
                 }
             }
-            prev_overflow = e1 - e0 > 32 * kSaved;
-            for (int e = e0 + 32 * kSaved + lane; e < e1; e += 32) {
+            prev_overflow = cur.e1 - cur.e0 > 32 * kSaved;
+            for (int e = cur.e0 + 32 * kSaved + lane; e < cur.e1; e += 32) {
                 const uint32_t en = __ldg(P.ents + e);
                 *reinterpret_cast<uint16_t*>(As + ent_offset(en)) = uint16_t(en >> 16);
             }
+            // every lane makes its writes visible to the tensor core's (async) reads, the warp
+            // barrier orders them before lane 0's arrival, which releases them to the MMA issuer
             fence_proxy_async_smem();
-            mbar_arrive(&full_a[s]);
-            kc = nkc;
-            e0 = ne0;
-            e1 = ne1;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_a[s]);
+            ++use;
+            return true;
+        };
+        for (;;) {
+            if (!step(X, Y, Z)) break;
+            if (!step(Y, Z, X)) break;
+            if (!step(Z, X, Y)) break;
         }
         __syncwarp();
-        // a B load that was issued must land before the CTA exits (normally it has been awaited
-        // by the MMA issuer already, and this wait returns at once)
+        // A B load that was issued must land before the CTA exits (normally the MMA warp has
+        // awaited it already and this returns at once).
         if (kTma && lane == 0 && last_use >= 0) mbar_wait_bounded(&full_b[s], uint32_t(last_use) & 1u);
-    } else if (warp == kMmaWarp && lane == 0) {
-        // ---- MMA issuer ----------------------------------------------------------------------
-        constexpr uint32_t kIdesc = idesc_f16_f32(kBandRows, kSlab, true);
-        int committed = -1;
-        for (int i = 0; i < nt; ++i) {
-            const int s = i % kStages;
-            const uint32_t par = uint32_t(i / kStages) & 1u;
-            bool good = mbar_wait_bounded(&full_a[s], par);
-            if (kTma && good) good = mbar_wait_bounded(&full_b[s], par);
-            if (!good) {
-                *abort_flag = 1;
-                atomicOr(P.status, kStatusTimeout);
-                break;
-            }
-            tc_fence_after();
-            const uint32_t a_addr = smem_u32(smem + s * kStageBytes + kBBytes);
-            const uint32_t b_addr = smem_u32(smem + s * kStageBytes);
-#pragma unroll
-            for (int kk = 0; kk < kBandK / 16; ++kk)
-                tc_mma_f16(tmem, smem_desc(a_addr + kk * 256, 128, kBandK * 16, 0),
-                           smem_desc(b_addr + kk * 2048, kPanelBytes, 1024, 2), kIdesc, (i > 0 || kk > 0) ? 1u : 0u);
-            tc_commit(&done[s]);
-            committed = i;
-        }
-        // the accumulator is complete (or, after a timeout, no MMA is in flight) once the last
-        // committed group of MMAs has completed
-        if (committed >= 0 && !mbar_wait_bounded(&done[committed % kStages], uint32_t(committed / kStages) & 1u)) {
-            *abort_flag = 1;
-            atomicOr(P.status, kStatusTimeout);
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-
-    // ---- epilogue: warp w < 4 holds rows 32w .. 32w+31 of the accumulator -----------------------
-    if (*abort_flag == 0 && warp < 4) {
-        const int grow = row0 + warp * 32 + lane;
-        float* crow = C + int64_t(grow) * ldc + k0;
-#pragma unroll 1
-        for (int c = 0; c < kSlab; c += 32) {
-            if (c >= ncols) break;  // uniform across the CTA
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c), v);
-            tmem_wait_ld();
-            if (grow < P.M) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int col = c + 4 * j;
-                    float4 x = make_float4(__uint_as_float(v[4 * j]) * P.scale, __uint_as_float(v[4 * j + 1]) * P.scale,
-                                           __uint_as_float(v[4 * j + 2]) * P.scale,
-                                           __uint_as_float(v[4 * j + 3]) * P.scale);
-                    if (vec_c && col + 3 < ncols) {
-                        float4* d = reinterpret_cast<float4*>(crow + col);
-                        if constexpr (kAcc) {
-                            const float4 o = *d;
-                            x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
-                        }
-                        __stcs(d, x);
-                    } else {
-                        const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            if (col + q < ncols) {
-                                if constexpr (kAcc) crow[col + q] += xs[q];
-                                else crow[col + q] = xs[q];
-                            }
+    } else if (warp == kMmaWarp) {
+        // ---- MMA issuer: the tile sequence in order, one accumulator per band -----------------
+        if (lane == 0) {
+            constexpr uint32_t kIdesc = idesc_f16_f32(kBandRows, kSlab, true);
+            uint32_t q = 0, u = 0;  // sequence position; bands with tiles so far
+            int last_stage = -1;
+            uint32_t last_par = 0;
+            bool ok = true;
+            ItemRange r = item_range(P, blockIdx.x, n_items);
+            for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+                const ItemRange rn = item_range(P, item + gridDim.x, n_items);
+                if (r.nt > 0) {
+                    const uint32_t acc = u % kAccs;
+                    if (u >= kAccs && !wait_or_abort(&acc_empty[acc], ((u / kAccs) - 1u) & 1u, abort_flag)) {
+                        ok = false;
+                        break;
                     }
+                    tc_fence_after();
+                    for (int t = 0; t < r.nt; ++t, ++q) {
+                        const int s = int(q % kStages);
+                        const uint32_t par = (q / kStages) & 1u;
+                        if (!wait_or_abort(&full_a[s], par, abort_flag) ||
+                            (kTma && !wait_or_abort(&full_b[s], par, abort_flag))) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = smem_u32(smem + s * kStageBytes + kBBytes);
+                        const uint32_t b_addr = smem_u32(smem + s * kStageBytes);
+#pragma unroll
+                        for (int kk = 0; kk < kBandK / 16; ++kk)
+                            tc_mma_f16(tmem + acc * kSlab, smem_desc(a_addr + kk * 256, 128, kBandK * 16, 0),
+                                       smem_desc(b_addr + kk * 2048, kPanelBytes, 1024, 2), kIdesc,
+                                       (t > 0 || kk > 0) ? 1u : 0u);
+                        tc_commit(&done[s]);
+                        last_stage = s;
+                        last_par = par;
+                    }
+                    if (!ok) break;
+                    tc_commit(&acc_full[acc]);
+                    ++u;
                 }
+                r = rn;
             }
+            // after an abort no MMA may still be reading shared memory or writing TMEM at exit
+            if (!ok && last_stage >= 0) mbar_wait_bounded(&done[last_stage], last_par);
+        }
+        __syncwarp();
+    } else {
+        // ---- epilogue: rows 32 q .. 32 q + 31 of each band, q = warp % 4 ------------------------
+        const int quarter = warp & 3;
+        const uint32_t lane_base = uint32_t(quarter * 32) << 16;
+        uint32_t u = 0;
+        ItemRange r = item_range(P, blockIdx.x, n_items);
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            const ItemRange rn = item_range(P, item + gridDim.x, n_items);
+            const int band = item % P.n_bands;
+            const int k0 = (item / P.n_bands) * kSlab;
+            const int ncols = min(kSlab, O - k0);
+            const int row0 = band * P.band_rows;
+            const int row_end = min(P.M, row0 + P.band_rows);
+            const int grow = row0 + quarter * 32 + lane;
+            float* crow = C + int64_t(grow) * ldc + k0;
+            if (r.nt == 0) {
+                if (!kAcc && grow < row_end)
+                    for (int c = 0; c < ncols; ++c) crow[c] = 0.f;
+            } else {
+                const uint32_t acc = u % kAccs;
+                if (!__all_sync(0xffffffffu, wait_or_abort(&acc_full[acc], (u / kAccs) & 1u, abort_flag))) break;
+                tc_fence_after();
+                // 32 rows x 32 columns at a time: TMEM -> registers (thread = row) -> shared
+                // memory -> registers (8 lanes = one 128-byte row segment) -> C, so that every
+                // warp store writes four whole 128-byte lines
+                float* stage_c = reinterpret_cast<float*>(smem + kEpiOffset + quarter * kEpiBytes);
+                const int nrows = min(32, row_end - (row0 + quarter * 32));  // may be <= 0
+#pragma unroll 1
+                for (int c = 0; c < kSlab; c += 32) {
+                    if (c >= ncols) break;
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem + lane_base + acc * kSlab + uint32_t(c), v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<float4*>(stage_c + lane * kEpiStride + 4 * j) =
+                            make_float4(__uint_as_float(v[4 * j]) * P.scale, __uint_as_float(v[4 * j + 1]) * P.scale,
+                                        __uint_as_float(v[4 * j + 2]) * P.scale,
+                                        __uint_as_float(v[4 * j + 3]) * P.scale);
+                    __syncwarp();
+                    const int cq = 4 * (lane & 7);  // this lane's 4 columns of a row segment
+                    const int col = c + cq;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int rr = 4 * i + (lane >> 3);
+                        if (rr < nrows) {
+                            float4 x = *reinterpret_cast<const float4*>(stage_c + rr * kEpiStride + cq);
+                            float* dst = C + int64_t(row0 + quarter * 32 + rr) * ldc + k0 + col;
+                            if (vec_c && col + 3 < ncols) {
+                                if constexpr (kAcc) {
+                                    const float4 o = *reinterpret_cast<const float4*>(dst);
+                                    x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+                                }
+                                __stcs(reinterpret_cast<float4*>(dst), x);
+                            } else {
+                                const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    if (col + k < ncols) {
+                                        if constexpr (kAcc) dst[k] += xs[k];
+                                        else dst[k] = xs[k];
+                                    }
+                            }
+                        }
+                    }
+                    __syncwarp();  // the staging tile is rewritten by the next 32 columns
+                }
+                tc_fence_before();
+                mbar_arrive(&acc_empty[acc]);
+                ++u;
+            }
+            r = rn;
         }
     }
     tc_fence_before();
     __syncthreads();
+    if (tid == 0 && *abort_flag != 0) atomicOr(P.status, kStatusTimeout);
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
@@ -313,12 +460,16 @@ template <bool kTma, bool kAcc, typename BT>
 cudaError_t launch_band_t(const BandPlanView& P, const CUtensorMap& tmap, const BT* B, int64_t ldb, int O, float* C,
                           int64_t ldc, cudaStream_t st) {
     auto kern = vcsr_band_kernel<kTma, kAcc, BT>;
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
+    int dev = 0, sms = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
     const int vec_c = ((ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) ? 1 : 0;
-    const int slabs = (O + kSlab - 1) / kSlab;
-    if (slabs > 65535) return cudaErrorInvalidValue;
-    const dim3 grid(unsigned(P.n_bands), unsigned(slabs));
+    const int64_t items = int64_t(P.n_bands) * ((O + kSlab - 1) / kSlab);
+    if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
+    // persistent: at most kCtasPerSm CTAs per SM, each walking its items in a strided order
+    const int grid = int(std::min<int64_t>(items, int64_t(sms) * kCtasPerSm));
     kern<<<grid, kThreads, kSmemBytes, st>>>(P, tmap, B, ldb, O, C, ldc, vec_c);
     return cudaGetLastError();
 }
@@ -347,34 +498,86 @@ cudaError_t spmm_band(const BandPlanView& P, const void* B, int b_is_f16, int64_
 }
 
 // ---- host: the band view -----------------------------------------------------------------------
-BandViewHost build_band_view(const RowViewHost& rv, int M, int nthreads) {
+namespace {
+
+// Sort key of an entry of a band: column, then row in the band, then the fp16 value bits.
+uint64_t band_key(int col, int row_in_band, float v) {
+    const __half hv = __float2half_rn(v);
+    unsigned short bits;
+    std::memcpy(&bits, &hv, sizeof bits);
+    return (uint64_t(uint32_t(col)) << 32) | (uint64_t(row_in_band) << 16) | bits;
+}
+
+// Greedy tiles over a band's keys sorted by column: a tile starts at the first column not yet
+// covered and covers 32 columns. Returns the number of tiles.
+int64_t count_tiles(const uint64_t* kb, const uint64_t* ke) {
+    int64_t n = 0;
+    int64_t end = -1;  // first column past the current tile
+    for (const uint64_t* k = kb; k < ke; ++k) {
+        const int64_t c = int64_t(*k >> 32);
+        if (c >= end) {
+            ++n;
+            end = c + kBandK;
+        }
+    }
+    return n;
+}
+
+void band_keys(const RowViewHost& rv, int r0, int r1, uint64_t* out) {
+    for (int r = r0; r < r1; ++r)
+        for (int p = rv.rp[r]; p < rv.rp[r + 1]; ++p) *out++ = band_key(rv.cols[p], r - r0, rv.vals[p]);
+}
+
+}  // namespace
+
+BandChoice choose_band(const RowViewHost& rv, int M) {
+    static const int kCandidates[] = {128, 127, 126, 124, 120, 112, 96, 64};
+    BandChoice best{kBandRows, 0.0};
+    double best_cost = 0.0;
+    std::vector<uint64_t> keys;
+    for (const int H : kCandidates) {
+        const int nb = (M + H - 1) / H;
+        if (nb == 0) return best;
+        const int samples = std::min(nb, 64);
+        int64_t tiles = 0, rows = 0, ents = 0;
+        for (int k = 0; k < samples; ++k) {
+            const int b = int(int64_t(k) * nb / samples);
+            const int r0 = b * H, r1 = std::min(M, r0 + H);
+            keys.resize(size_t(rv.rp[r1] - rv.rp[r0]));
+            band_keys(rv, r0, r1, keys.data());
+            std::sort(keys.begin(), keys.end());
+            tiles += count_tiles(keys.data(), keys.data() + keys.size());
+            rows += r1 - r0;
+            ents += int64_t(keys.size());
+        }
+        // tensor-core tiles per row, plus the epilogue of a band (about two tiles' time)
+        const double cost = (double(tiles) + 2.0 * samples) / double(std::max<int64_t>(rows, 1));
+        if (H == kCandidates[0] || cost < best_cost * 0.995) {
+            best_cost = cost;
+            best = BandChoice{H, tiles > 0 ? double(ents) / double(tiles) : 0.0};
+        }
+    }
+    return best;
+}
+
+BandViewHost build_band_view(const RowViewHost& rv, int M, int band_rows, int nthreads) {
+    if (band_rows < 1 || band_rows > kBandRows) throw StatusError(VCSRMC_INTERNAL, "band height out of range");
     BandViewHost h;
-    const int nb = (M + kBandRows - 1) / kBandRows;
+    h.band_rows = band_rows;
+    const int H = band_rows;
+    const int nb = (M + H - 1) / H;
     const int64_t nnz = M > 0 ? rv.rp[M] : 0;
-    // one sort key per entry: tile (column / 32) above (row in band, local column, fp16 value),
-    // so a band's sorted keys are its tiles in column order
     std::vector<uint64_t> keys(size_t(std::max<int64_t>(nnz, 0)));
     std::vector<int> ntiles(size_t(nb), 0);
     const int nth = resolve_threads(nthreads);
     parallel_for_dynamic(0, nb, nth, 64, [&](int64_t lo, int64_t hi) {
         for (int64_t b = lo; b < hi; ++b) {
-            const int r0 = int(b) * kBandRows, r1 = std::min(M, r0 + kBandRows);
-            for (int r = r0; r < r1; ++r)
-                for (int p = rv.rp[r]; p < rv.rp[r + 1]; ++p) {
-                    const uint32_t col = uint32_t(rv.cols[p]);
-                    const __half hv = __float2half_rn(rv.vals[p]);
-                    unsigned short bits;
-                    std::memcpy(&bits, &hv, sizeof bits);
-                    const uint32_t ent = (col & 31u) | (uint32_t(r - r0) << 5) | (uint32_t(bits) << 16);
-                    keys[size_t(p)] = (uint64_t(col >> 5) << 32) | ent;
-                }
+            const int r0 = int(b) * H, r1 = std::min(M, r0 + H);
             uint64_t* kb = keys.data() + rv.rp[r0];
             uint64_t* ke = keys.data() + rv.rp[r1];
+            band_keys(rv, r0, r1, kb);
             std::sort(kb, ke);
-            int n = 0;
-            for (uint64_t* k = kb; k < ke; ++k)
-                if (k == kb || (*k >> 32) != (k[-1] >> 32)) ++n;
-            ntiles[size_t(b)] = n;
+            ntiles[size_t(b)] = int(count_tiles(kb, ke));
         }
     });
     h.tile_ptr.assign(size_t(nb) + 1, 0);
@@ -386,16 +589,21 @@ BandViewHost build_band_view(const RowViewHost& rv, int M, int nthreads) {
     h.tile_eptr[size_t(T)] = int(nnz);
     parallel_for_dynamic(0, nb, nth, 64, [&](int64_t lo, int64_t hi) {
         for (int64_t b = lo; b < hi; ++b) {
-            const int r0 = int(b) * kBandRows, r1 = std::min(M, r0 + kBandRows);
-            int t = h.tile_ptr[size_t(b)];
+            const int r0 = int(b) * H, r1 = std::min(M, r0 + H);
+            int t = h.tile_ptr[size_t(b)] - 1;
+            int64_t end = -1, start = 0;
             for (int p = rv.rp[r0]; p < rv.rp[r1]; ++p) {
                 const uint64_t k = keys[size_t(p)];
-                if (p == rv.rp[r0] || (k >> 32) != (keys[size_t(p) - 1] >> 32)) {
-                    h.tile_col[size_t(t)] = int(k >> 32) * kBandK;
-                    h.tile_eptr[size_t(t)] = p;
+                const int64_t c = int64_t(k >> 32);
+                if (c >= end) {  // a new tile starts at this column
                     ++t;
+                    start = c;
+                    end = c + kBandK;
+                    h.tile_col[size_t(t)] = int(c);
+                    h.tile_eptr[size_t(t)] = p;
                 }
-                h.ents[size_t(p)] = uint32_t(k);
+                const uint32_t row = uint32_t(k >> 16) & 0x7fu, bits = uint32_t(k & 0xffffu);
+                h.ents[size_t(p)] = uint32_t(c - start) | (row << 5) | (bits << 16);
             }
         }
     });
@@ -404,11 +612,12 @@ BandViewHost build_band_view(const RowViewHost& rv, int M, int nthreads) {
     for (int b = 0; b < nb; ++b) {
         const int t0 = h.tile_ptr[size_t(b)], t1 = h.tile_ptr[size_t(b) + 1];
         if (t1 < t0 || t1 > T) bad();
-        const int r0 = b * kBandRows, r1 = std::min(M, r0 + kBandRows);
+        const int r0 = b * H, r1 = std::min(M, r0 + H);
         if (t1 > t0 && (h.tile_eptr[size_t(t0)] != rv.rp[r0] || h.tile_eptr[size_t(t1)] != rv.rp[r1])) bad();
+        if (t1 == t0 && rv.rp[r1] != rv.rp[r0]) bad();
         for (int t = t0; t < t1; ++t)
             if (h.tile_eptr[size_t(t) + 1] <= h.tile_eptr[size_t(t)] || h.tile_col[size_t(t)] < 0 ||
-                h.tile_col[size_t(t)] % kBandK != 0 || (t > t0 && h.tile_col[size_t(t)] <= h.tile_col[size_t(t) - 1]))
+                (t > t0 && h.tile_col[size_t(t)] < h.tile_col[size_t(t) - 1] + kBandK))
                 bad();
     }
     return h;

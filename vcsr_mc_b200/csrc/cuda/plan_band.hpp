@@ -10,29 +10,42 @@
 namespace vcsrmc {
 namespace dev {
 
-constexpr int kBandRows = 128;  // rows per band = tcgen05 tile M
+constexpr int kBandRows = 128;  // rows per band at most = tcgen05 tile M
 constexpr int kBandK = 32;      // columns of A (= rows of B) per tile: two K = 16 MMA steps
+// Below this many entries per tile the ROWS plan is faster (measured on a B200: about 1.1 ns of
+// tensor-core pipeline per tile against 0.025-0.045 ns per gathered entry for ROWS).
+constexpr double kBandMinEntriesPerTile = 40.0;
 
-// Host-side band view. Band b covers rows [128 b, 128 b + 128). Its tiles are
+// Host-side band view. Band b covers rows [b * band_rows, (b + 1) * band_rows). Its tiles are
 // [tile_ptr[b], tile_ptr[b+1]) in ascending column order; tile t covers columns
-// [tile_col[t], tile_col[t] + 32) and holds entries [tile_eptr[t], tile_eptr[t+1]).
-// An entry packs the local column (bits 0-4), the row within the band (bits 5-11) and the
-// fp16 value (bits 16-31).
+// [tile_col[t], tile_col[t] + 32) and holds entries [tile_eptr[t], tile_eptr[t+1]). A tile starts
+// at the first column of the band not covered by the previous tile, so a window of w
+// consecutive occupied columns takes ceil(w / 32) tiles wherever it starts. An entry packs the
+// local column (bits 0-4), the row within the band (bits 5-11) and the fp16 value (bits 16-31).
 struct BandViewHost {
+    int band_rows = kBandRows;
     std::vector<int> tile_ptr, tile_col, tile_eptr;
     std::vector<uint32_t> ents;
 };
 
+// The band height (<= 128) that minimises tiles per row (plus a per-band cost), estimated on a
+// sample of bands, and the mean entries per tile it gives.
+struct BandChoice {
+    int band_rows;
+    double entries_per_tile;
+};
+BandChoice choose_band(const RowViewHost& rv, int M);
+
 // From the row view (rows' entries in ascending column order, values already divided by the
 // format's scale). nthreads <= 0: all host threads.
-BandViewHost build_band_view(const RowViewHost& rv, int M, int nthreads);
+BandViewHost build_band_view(const RowViewHost& rv, int M, int band_rows, int nthreads);
 
 struct BandPlanView {
     const int* tile_ptr;
     const int* tile_col;
     const int* tile_eptr;
     const uint32_t* ents;
-    int n_bands;
+    int n_bands, band_rows;
     int M, N;
     float scale;
     uint32_t* status;
