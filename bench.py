@@ -237,6 +237,48 @@ def time_cusparse(rp, col, val, r0, r1, p0, p1, N, B, fp16: bool, stream) -> dic
 
 
 # ---------------------------------------------------------------------------------------------
+def shard_balance(args, spec: dict, fp16: bool) -> None:
+    """Per-shard SpMM times of N-way row partitions, measured shard by shard on one GPU."""
+    import torch
+    import vcsr_mc_b200 as vm
+    M, N, rp, col, val = load_or_generate_csr(spec, 0, 1, lambda: None)
+    rp32 = np.asarray(rp, dtype=np.int32)
+    plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND}[args.plan]
+    B = torch.empty((N, O_COLS), dtype=torch.float16 if fp16 else torch.float32, device="cuda")
+    vm.gen_dense_device(B, SEED)
+
+    def shard_ms(r0: int, r1: int) -> float:
+        p0, p1 = int(rp[r0]), int(rp[r1])
+        S = vm.CSR.from_arrays(r1 - r0, N, np.asarray(rp[r0:r1 + 1], dtype=np.int64) - p0,
+                               np.asarray(col[p0:p1]), np.asarray(val[p0:p1]))
+        dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(S, fp32=not fp16, segw=args.segw), device=0, plans=[plan])
+        C = torch.empty((max(r1 - r0, 1), O_COLS), dtype=torch.float32, device="cuda")
+        for _ in range(args.warmup):
+            vm.spmm(dV, B, C, tileK=args.tileK, plan=plan)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            vm.spmm(dV, B, C, tileK=args.tileK, plan=plan)
+        b.record()
+        torch.cuda.synchronize()
+        dV.free()
+        return a.elapsed_time(b) / args.steps
+
+    full = shard_ms(0, M)
+    out = {"mode": "shard_balance", "workload": spec["desc"], "dtype": args.dtype, "plan": args.plan,
+           "one_gpu_ms": full, "partitions": []}
+    for world in [int(x) for x in args.shard_balance.split(",") if x]:
+        for w in [float(x) for x in args.row_weights.split(",") if x]:
+            cuts = vm.partition_rows(rp32, world, row_weight=w)
+            ms = [shard_ms(int(cuts[k]), int(cuts[k + 1])) for k in range(world)]
+            out["partitions"].append({"gpus": world, "row_weight": w, "shard_ms": ms,
+                                      "predicted_efficiency": full / (world * max(ms))})
+            log(f"{world} GPUs, row weight {w}: shards {[round(x, 3) for x in ms]} "
+                f"-> efficiency {full / (world * max(ms)):.3f}")
+    emit(out)
+
+
 def main() -> None:
     # Only the result line goes to stdout: everything else (libraries included, e.g. NCCL's
     # version banner) is sent to stderr at the file-descriptor level.
@@ -260,10 +302,17 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
     ap.add_argument("--cpu-sample-nnz", type=int, default=8_000_000)
+    ap.add_argument("--build", choices=["host", "device"], default="host",
+                    help="format construction: host (bit-identical to the reference builder) or device (GPU)")
     ap.add_argument("--unit-nnz", type=int, default=0,
                     help="ROWS plan: entries per work unit (0 = the library's choice for the matrix)")
     ap.add_argument("--row-weight", type=float, default=5.4,
                     help="shard balance: cost = nnz + row_weight * rows (0 = nnz balance)")
+    ap.add_argument("--shard-balance", default="",
+                    help="e.g. 2,4,8: time every shard of each N-way row partition one after another on this "
+                         "GPU (the path has no collective, so the slowest shard predicts the N-GPU step) and "
+                         "print that instead of the bench line")
+    ap.add_argument("--row-weights", default="0,5.4,10", help="row weights tried by --shard-balance")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -280,6 +329,10 @@ def main() -> None:
                        "band": "band: 128-row bands x 32-column tiles on tcgen05, TMEM accumulator, C stored once"}[args.plan],
               "parallelism": f"row-shard x{args.gpus} (balanced on nnz + {args.row_weight} x rows), B replicated",
               "l2": None}
+
+    if args.shard_balance:
+        shard_balance(args, spec, fp16)
+        return
 
     if args.impl == "reference":
         # The reference's own CPU implementation of the path (oracle/_ref), rank 0 only.
@@ -324,21 +377,32 @@ def main() -> None:
     shard = vm.CSR.from_arrays(r1 - r0, N, np.asarray(rp[r0:r1 + 1], dtype=np.int64) - p0,
                                np.asarray(col[p0:p1]), np.asarray(val[p0:p1]))
     nthreads = max(1, cores // world)
+    plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND}[args.plan]
+    torch.cuda.synchronize()
     tb = time.time()
-    V = vm.csr_to_vcsr_mc(shard, fp32=not fp16, segw=args.segw, nthreads=nthreads)
+    if args.build == "device":
+        # the shard's CSR goes to the GPU once and the format is built there
+        d_rp = torch.from_numpy(np.asarray(shard.arrays(copy=False)[0])).cuda()
+        d_col = torch.from_numpy(np.asarray(shard.arrays(copy=False)[1])).cuda()
+        d_val = torch.from_numpy(np.asarray(shard.arrays(copy=False)[2])).cuda()
+        dV = vm.build_vcsr_mc_device(d_rp, d_col, d_val, shard.M, shard.N, fp32=not fp16, segw=args.segw,
+                                     device=local, plans=[plan], rows_unit_nnz=args.unit_nnz)
+        del d_rp, d_col, d_val
+    else:
+        V = vm.csr_to_vcsr_mc(shard, fp32=not fp16, segw=args.segw, nthreads=nthreads)
+        dV = vm.upload_vcsr_mc_device(V, device=local, plans=[plan], rows_unit_nnz=args.unit_nnz)
+        del V
+    torch.cuda.synchronize()
     build_s = time.time() - tb
     D = int(np.unique(np.asarray(col[p0:p1])).size) if p1 > p0 else 0
-    plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND}[args.plan]
-    dV = vm.upload_vcsr_mc_device(V, device=local, plans=[plan], rows_unit_nnz=args.unit_nnz)
     Ms = r1 - r0
-    # this library's kernels per step: the SpMM kernel, plus (ROWS plan) the zeroing of rows
-    # longer than one 256-entry work unit, whose chunks are reduced into C
-    heavy = int(np.count_nonzero(np.diff(np.asarray(rp[r0:r1 + 1], dtype=np.int64)) > 256))
-    launches_per_step = 1 + (1 if plan == vm.PLAN_ROWS and heavy > 0 else 0)
-    groups, slots, items = V.n_groups, V.n_slots, V.n_items
-    del V
-    log(f"rank {rank}: rows [{r0},{r1}) nnz {p1 - p0} groups {groups} slots {slots} items {items} "
-        f"build {build_s:.1f}s setup {time.time() - t0:.1f}s")
+    info = dV.info()
+    # this library's kernels per step: the SpMM kernel, plus (ROWS plan) the zeroing of the rows
+    # split into chunks that are reduced into C
+    launches_per_step = 1 + (1 if plan == vm.PLAN_ROWS and info["n_split_rows"] > 0 else 0)
+    groups, slots, items = info["n_groups"], info["n_slots"], info["n_items"]
+    log(f"rank {rank}: rows [{r0},{r1}) nnz {p1 - p0} format build + upload ({args.build}) {build_s:.2f}s "
+        f"setup {time.time() - t0:.1f}s")
 
     dt = torch.float16 if fp16 else torch.float32
     B = torch.empty((N, O_COLS), dtype=dt, device="cuda")
@@ -503,6 +567,8 @@ def main() -> None:
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "detail": {"nnz": nnz_total, "M": M, "N": N, "rank0_rows": Ms, "rank0_distinct_cols": D,
                        "groups": groups, "slots": slots, "items": items, "device_status": status,
+                       "format_build": args.build, "format_build_upload_s": build_s,
+                       "rows_unit_nnz": info["rows_unit_nnz"], "band_rows": info["band_rows"],
                        "clock_samples": clk["samples"]},
         }
         emit(line)

@@ -151,7 +151,32 @@ typedef struct {
 } vcsrmc_upload_options;
 int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const vcsrmc_upload_options* opts,
                        void* stream, vcsrmc_device_format** out);
+/* Device-side construction: builds the format of a CSR already in device memory (row_ptr[M+1],
+ * col[nnz], val[nnz] on `device`; row_ptr from 0 to nnz, rows with strictly ascending columns)
+ * and makes its plan layouts resident there, without a host copy of the matrix. opts may be NULL;
+ * plans 0 = SEGMENT and ROWS (a BAND layout, when asked for, is built on the host from a copy).
+ * Rows with equal per-segment entry counts are ordered by ascending row, so group_rows, lcol and
+ * val can differ from vcsrmc_build_host's by a permutation inside such runs (the reference takes
+ * that order from its hash map); every other array is identical. Blocking. */
+int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const int32_t* row_ptr, const int32_t* col,
+                        const float* val, int fp32, int segw, int device,
+                        const vcsrmc_upload_options* opts, void* stream, vcsrmc_device_format** out);
+/* Copies the SEGMENT arrays of a device format back into a host format (values as the device
+ * holds them: FP16 formats keep them rounded to fp16). */
+int vcsrmc_device_download(const vcsrmc_device_format* d, vcsrmc_format** out);
 int vcsrmc_device_free(vcsrmc_device_format* d);
+/* Shape and resident layouts of a device format. */
+typedef struct {
+    int32_t device, M, N, segw, fp32;
+    float scale;
+    int32_t plans;                        /* resident layouts: bits (1 << VCSRMC_PLAN_*)     */
+    int64_t n_groups, n_slots, n_items;   /* SEGMENT layout                                 */
+    int64_t n_units;                      /* ROWS layout: work units                        */
+    int32_t rows_unit_nnz, n_split_rows;  /* ROWS: entries per unit, rows split into chunks */
+    int32_t band_rows, n_bands;           /* BAND layout                                    */
+    int64_t n_tiles;
+} vcsrmc_device_info;
+int vcsrmc_device_info_get(const vcsrmc_device_format* d, vcsrmc_device_info* out);
 /* Error flags raised by kernels of this format since the last clear (bit 0: a bounded wait
  * timed out). Blocking read. */
 int vcsrmc_device_status(const vcsrmc_device_format* d, uint32_t* flags, int clear);

@@ -32,6 +32,15 @@ class VcsrmcError(RuntimeError):
         super().__init__(f"{_STATUS_NAMES.get(status, status)}: {message}")
 
 
+class DeviceInfo(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int32), ("M", ctypes.c_int32), ("N", ctypes.c_int32), ("segw", ctypes.c_int32),
+                ("fp32", ctypes.c_int32), ("scale", ctypes.c_float), ("plans", ctypes.c_int32),
+                ("n_groups", ctypes.c_int64), ("n_slots", ctypes.c_int64), ("n_items", ctypes.c_int64),
+                ("n_units", ctypes.c_int64), ("rows_unit_nnz", ctypes.c_int32), ("n_split_rows", ctypes.c_int32),
+                ("band_rows", ctypes.c_int32), ("n_bands", ctypes.c_int32),
+                ("n_tiles", ctypes.c_int64)]
+
+
 class UploadOptions(ctypes.Structure):
     _fields_ = [("plans", ctypes.c_int32), ("rows_unit_nnz", ctypes.c_int32), ("band_rows", ctypes.c_int32),
                 ("reserved", ctypes.c_int32 * 5)]
@@ -84,6 +93,10 @@ PROTOTYPES = {
     "vcsrmc_upload": (_int, [_p, _int, _p, _pp]),
     "vcsrmc_upload_ex": (_int, [_p, _int, _int, _p, _pp]),
     "vcsrmc_upload_opts": (_int, [_p, _int, ctypes.POINTER(UploadOptions), _p, _pp]),
+    "vcsrmc_build_device": (_int, [_i32, _i32, _i64, _p, _p, _p, _int, _int, _int, ctypes.POINTER(UploadOptions), _p,
+                                   _pp]),
+    "vcsrmc_device_download": (_int, [_p, _pp]),
+    "vcsrmc_device_info_get": (_int, [_p, ctypes.POINTER(DeviceInfo)]),
     "vcsrmc_device_free": (_int, [_p]),
     "vcsrmc_device_status": (_int, [_p, ctypes.POINTER(ctypes.c_uint32), _int]),
     "vcsrmc_spmm": (_int, [_p, _p, _int, _i64, _i32, _i32, _p, _i64, _int, _p]),

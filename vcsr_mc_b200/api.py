@@ -20,7 +20,7 @@ from typing import Optional
 import numpy as np
 
 from . import _lib
-from ._lib import F16, F32, PLAN_AUTO, PLAN_ROWS, PLAN_SEGMENT, VcsrmcError, call
+from ._lib import F16, F32, PLAN_AUTO, PLAN_BAND, PLAN_ROWS, PLAN_SEGMENT, VcsrmcError, call
 
 
 def _ptr(a: np.ndarray) -> ctypes.c_void_p:
@@ -186,11 +186,26 @@ def _stream_handle(stream) -> ctypes.c_void_p:
 class DeviceVCSRMC:
     """A VCSR-MC format resident on one GPU (replaces src/vcsr_mc.cu:126-131's statics)."""
 
-    def __init__(self, handle: ctypes.c_void_p, host: VCSRMC, device: int):
+    def __init__(self, handle: ctypes.c_void_p, host: Optional[VCSRMC], device: int, **shape):
         self._h = handle
         self.device = device
-        self.M, self.N, self.fp32, self.scale, self.segw = host.M, host.N, host.fp32, host.scale, host.segw
-        self.n_groups, self.n_slots, self.n_items = host.n_groups, host.n_slots, host.n_items
+        if host is not None:
+            shape = dict(M=host.M, N=host.N, fp32=host.fp32, scale=host.scale, segw=host.segw)
+        self.M, self.N, self.fp32, self.scale, self.segw = (shape[k] for k in ("M", "N", "fp32", "scale", "segw"))
+
+    def info(self) -> dict:
+        """Shape and resident layouts (vcsrmc_device_info_get); plans is a list of PLAN_* values."""
+        i = _lib.DeviceInfo()
+        call("vcsrmc_device_info_get", self._h, ctypes.byref(i))
+        out = {k: getattr(i, k) for k, _ in _lib.DeviceInfo._fields_}
+        out["plans"] = [p for p in (PLAN_SEGMENT, PLAN_ROWS, PLAN_BAND) if i.plans & (1 << p)]
+        return out
+
+    def download(self) -> VCSRMC:
+        """The SEGMENT arrays back on the host (FP16 formats: values as stored, rounded to fp16)."""
+        h = ctypes.c_void_p()
+        call("vcsrmc_device_download", self._h, ctypes.byref(h))
+        return VCSRMC(h)
 
     @property
     def handle(self) -> ctypes.c_void_p:
@@ -226,6 +241,29 @@ def upload_vcsr_mc_device(V: VCSRMC, device: int = 0, stream=None, plans=None,
     h = ctypes.c_void_p()
     call("vcsrmc_upload_opts", V.handle, device, ctypes.byref(opts), _stream_handle(stream), ctypes.byref(h))
     return DeviceVCSRMC(h, V, device)
+
+
+def build_vcsr_mc_device(row_ptr, col, val, M: int, N: int, fp32: bool = False, segw: int = 16, device: int = 0,
+                         stream=None, plans=None, rows_unit_nnz: int = 0, band_rows: int = 0) -> DeviceVCSRMC:
+    """Builds the format on the GPU from a CSR already in device memory (torch tensors: int32
+    row_ptr[M+1], int32 col[nnz], float32 val[nnz], rows with strictly ascending columns) and
+    keeps its plan layouts resident there. Equal-count rows of a segment come in ascending row
+    order (see vcsrmc_build_device)."""
+    import torch
+    for t, dt in ((row_ptr, torch.int32), (col, torch.int32), (val, torch.float32)):
+        if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == dt and t.is_contiguous()):
+            raise VcsrmcError(_lib.INVALID_ARG, "row_ptr/col/val must be contiguous CUDA tensors (int32, int32, float32)")
+    opts = _lib.UploadOptions()
+    opts.plans = 0 if plans is None else sum(1 << p for p in set(plans))
+    opts.rows_unit_nnz = rows_unit_nnz
+    opts.band_rows = band_rows
+    h = ctypes.c_void_p()
+    call("vcsrmc_build_device", M, N, int(col.numel()), ctypes.c_void_p(row_ptr.data_ptr()),
+         ctypes.c_void_p(col.data_ptr()), ctypes.c_void_p(val.data_ptr()), 1 if fp32 else 0, segw, device,
+         ctypes.byref(opts), _stream_handle(stream), ctypes.byref(h))
+    info = _lib.DeviceInfo()
+    call("vcsrmc_device_info_get", h, ctypes.byref(info))
+    return DeviceVCSRMC(h, None, device, M=M, N=N, fp32=fp32, scale=float(info.scale), segw=segw)
 
 
 def destroy_vcsr_mc_device(dV: DeviceVCSRMC) -> None:

@@ -21,6 +21,9 @@ struct vcsrmc_format {
 
 namespace vcsrmc {
 
+// half_scale (src/vcsr_mc.cu:14-22) from the largest |value|, shared by the host and device builders.
+float half_scale_from_absmax(float amax);
+
 // Thread-local last error, reported through vcsrmc_last_error().
 void set_last_error(int status, const std::string& msg);
 int fail(int status, const std::string& msg);

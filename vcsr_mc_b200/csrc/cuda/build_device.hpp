@@ -1,0 +1,55 @@
+// GPU-side construction of the VCSR-MC format and of the ROWS plan's row view from a CSR that is
+// already in device memory (see build_device.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace vcsrmc {
+namespace dev {
+
+// Device arrays of the SEGMENT plan, in the layout device_api.cu uploads (the caller owns them).
+struct SegmentLayout {
+    int2* items = nullptr;   // {gbeg, gend}
+    int4* gmeta = nullptr;   // {slot_begin, depth, seg_base, 0}
+    int* grows = nullptr;    // 16 per group, -1 = padding
+    int8_t* lcol = nullptr;  // per slot, -1 = padding
+    void* val = nullptr;     // per slot: __half (FP16 format) or float (FP32 format)
+    int64_t n_groups = 0, n_slots = 0, n_items = 0;
+    int num_segments = 0;
+};
+
+// Device arrays of the ROWS plan (the caller owns them).
+struct RowsLayout {
+    int* rp = nullptr;
+    int* cols = nullptr;
+    void* vals = nullptr;  // __half (FP16 format) or float
+    int4* units = nullptr;
+    int64_t n_units = 0;
+    int* split_rows = nullptr;
+    int n_split_rows = 0;
+};
+
+// Largest |val| (exact); the FP16 scale follows from it as in half_scale.
+float device_abs_max(const float* val, int64_t nnz, cudaStream_t st);
+
+// Checks row_ptr (0 first, non-decreasing, nnz last) and that every row's columns are strictly
+// ascending and inside [0, N). Returns false otherwise (blocking).
+bool device_csr_rows_sorted(const int* row_ptr, const int* col, int M, int N, int64_t nnz, cudaStream_t st);
+
+// The VCSR-MC arrays of csr_to_vcsr_mc (src/vcsr_mc.cu:25-123) with equal-count rows of a
+// segment in ascending row order. Throws StatusError on failure (nothing is leaked).
+SegmentLayout build_segment_layout(const int* row_ptr, const int* col, const float* val, int M, int N, int64_t nnz,
+                                   int segw, bool fp32, float scale, cudaStream_t st);
+
+// The row view: the CSR itself (rows sorted by column are already in the format's entry order),
+// values divided by the scale, and work units of at most unit_nnz entries packed inside aligned
+// blocks of 16 rows.
+RowsLayout build_rows_layout(const int* row_ptr, const int* col, const float* val, int M, int64_t nnz, bool fp32,
+                             float scale, int unit_nnz, cudaStream_t st);
+
+// Checks the invariants the SpMM kernels rely on (index ranges, offsets, item ranges). Blocking.
+bool device_validate(const SegmentLayout* seg, const RowsLayout* rows, int M, int N, int segw, cudaStream_t st);
+
+}  // namespace dev
+}  // namespace vcsrmc

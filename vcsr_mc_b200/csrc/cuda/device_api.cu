@@ -25,13 +25,14 @@
 #include "../common/vrng.h"
 #include "../host/parallel.hpp"
 #include "common.cuh"
+#include "build_device.hpp"
 #include "plan_band.hpp"
 #include "plan_rows.hpp"
 #include "spmm_launch.hpp"
 
 struct vcsrmc_device_format {
     int device = 0;
-    int M = 0, N = 0, segw = 0, fp32 = 0;
+    int M = 0, N = 0, segw = 0, fp32 = 0, num_segments = 0;
     float scale = 1.f;
     int64_t n_groups = 0, n_slots = 0, n_items = 0;
     int2* items = nullptr;
@@ -50,6 +51,7 @@ struct vcsrmc_device_format {
     void* rvals = nullptr;
     int* split_rows = nullptr;
     int n_split_rows = 0;
+    int unit_nnz = 0;
     // BAND plan
     bool has_band = false;
     int n_bands = 0, band_rows = 0;
@@ -314,6 +316,7 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
         d->M = v.M;
         d->N = v.N;
         d->segw = v.segw;
+        d->num_segments = v.num_segments;
         d->fp32 = v.fp32 ? 1 : 0;
         d->scale = v.scale;
         d->n_groups = int64_t(v.group_depth.size());
@@ -385,6 +388,7 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
                 d->n_units = int64_t(rv.units.size());
                 d->split_rows = upload_array(rv.split_rows.data(), rv.split_rows.size(), st);
                 d->n_split_rows = int(rv.split_rows.size());
+                d->unit_nnz = unit_nnz;
                 if (d->fp32) {
                     d->rvals = upload_array(rv.vals.data(), rv.vals.size(), st);
                 } else {
@@ -421,6 +425,31 @@ VCSRMC_EXPORT int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream
 
 VCSRMC_EXPORT int vcsrmc_device_free(vcsrmc_device_format* d) {
     return guarded([&] { free_device(d); });
+}
+
+VCSRMC_EXPORT int vcsrmc_device_info_get(const vcsrmc_device_format* d, vcsrmc_device_info* out) {
+    return guarded([&] {
+        if (!d || !out) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        vcsrmc_device_info i{};
+        i.device = d->device;
+        i.M = d->M;
+        i.N = d->N;
+        i.segw = d->segw;
+        i.fp32 = d->fp32;
+        i.scale = d->scale;
+        i.plans = (d->has_segment ? 1 << VCSRMC_PLAN_SEGMENT : 0) | (d->has_rows ? 1 << VCSRMC_PLAN_ROWS : 0) |
+                  (d->has_band ? 1 << VCSRMC_PLAN_BAND : 0);
+        i.n_groups = d->n_groups;
+        i.n_slots = d->n_slots;
+        i.n_items = d->n_items;
+        i.n_units = d->n_units;
+        i.rows_unit_nnz = d->unit_nnz;
+        i.n_split_rows = d->n_split_rows;
+        i.band_rows = d->band_rows;
+        i.n_bands = d->n_bands;
+        i.n_tiles = d->n_tiles;
+        *out = i;
+    });
 }
 
 VCSRMC_EXPORT int vcsrmc_device_status(const vcsrmc_device_format* d, uint32_t* flags, int clear) {
@@ -486,5 +515,182 @@ VCSRMC_EXPORT int vcsrmc_gen_dense_device(int64_t rows, int32_t cols, uint64_t s
         cuda_check(dev::gen_dense_device(rows, cols, seed, dtype == VCSRMC_F16 ? 1 : 0, out, ld,
                                          static_cast<cudaStream_t>(stream)),
                    "gen_dense_device");
+    });
+}
+
+VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const int32_t* row_ptr, const int32_t* col,
+                                      const float* val, int fp32, int segw, int device,
+                                      const vcsrmc_upload_options* opts, void* stream, vcsrmc_device_format** out) {
+    return guarded([&] {
+        if (!out) throw StatusError(VCSRMC_INVALID_ARG, "NULL output");
+        if (segw != 16 && segw != 32 && segw != 48 && segw != 64)
+            throw StatusError(VCSRMC_INVALID_ARG, "vcsr_mc supports segw in {16, 32, 48, 64}");
+        if (M < 0 || N < 0 || nnz < 0 || nnz > INT32_MAX) throw StatusError(VCSRMC_INVALID_ARG, "bad CSR sizes");
+        if (!row_ptr || (nnz > 0 && (!col || !val))) throw StatusError(VCSRMC_INVALID_ARG, "NULL CSR array");
+        vcsrmc_upload_options o{};
+        if (opts) o = *opts;
+        for (int r : o.reserved)
+            if (r != 0) throw StatusError(VCSRMC_INVALID_ARG, "reserved upload options must be 0");
+        int plans = o.plans == 0 ? ((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS)) : o.plans;
+        if (plans & ~((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS) | (1 << VCSRMC_PLAN_BAND)))
+            throw StatusError(VCSRMC_INVALID_ARG, "unknown plan bits");
+        if ((plans & (1 << VCSRMC_PLAN_BAND)) && fp32)
+            throw StatusError(VCSRMC_INVALID_ARG, "the BAND plan runs on the tensor cores and needs the FP16 format");
+        int unit_nnz = o.rows_unit_nnz;
+        if (unit_nnz != 0 && (unit_nnz < 16 || unit_nnz > dev::kUnitNnzMax || (unit_nnz & (unit_nnz - 1))))
+            throw StatusError(VCSRMC_INVALID_ARG, "rows_unit_nnz must be 0 or a power of two in [16, 1024]");
+        if (o.band_rows < 0 || o.band_rows > dev::kBandRows)
+            throw StatusError(VCSRMC_INVALID_ARG, "band_rows must be 0 or in [1, 128]");
+        if (device < 0) cuda_check(cudaGetDevice(&device), "cudaGetDevice");
+        DeviceGuard guard(device);
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (!dev::device_csr_rows_sorted(row_ptr, col, M, N, nnz, st))
+            throw StatusError(VCSRMC_INVALID_ARG,
+                              "the device builder needs row_ptr from 0 to nnz and rows with strictly ascending "
+                              "columns in [0, N) (vcsrmc_build_host sorts other rows)");
+        const float scale = fp32 ? 1.0f : half_scale_from_absmax(dev::device_abs_max(val, nnz, st));
+        auto* d = new vcsrmc_device_format;
+        d->device = device;
+        d->M = M;
+        d->N = N;
+        d->segw = segw;
+        d->num_segments = (N + segw - 1) / segw;
+        d->fp32 = fp32 ? 1 : 0;
+        d->scale = scale;
+        try {
+            dev::SegmentLayout seg;
+            dev::RowsLayout rows;
+            if (plans & (1 << VCSRMC_PLAN_SEGMENT)) {
+                seg = dev::build_segment_layout(row_ptr, col, val, M, N, nnz, segw, fp32 != 0, scale, st);
+                d->items = seg.items;
+                d->gmeta = seg.gmeta;
+                d->grows = seg.grows;
+                d->lcol = seg.lcol;
+                d->val = seg.val;
+                d->n_groups = seg.n_groups;
+                d->n_slots = seg.n_slots;
+                d->n_items = seg.n_items;
+                d->has_segment = true;
+            }
+            if (plans & (1 << VCSRMC_PLAN_ROWS)) {
+                if (unit_nnz == 0) {
+                    int sms = 0;
+                    cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device),
+                               "cudaDeviceGetAttribute");
+                    unit_nnz = dev::choose_unit_nnz(nnz, sms);
+                }
+                rows = dev::build_rows_layout(row_ptr, col, val, M, nnz, fp32 != 0, scale, unit_nnz, st);
+                d->rp = rows.rp;
+                d->cols = rows.cols;
+                d->rvals = rows.vals;
+                d->units = rows.units;
+                d->n_units = rows.n_units;
+                d->split_rows = rows.split_rows;
+                d->n_split_rows = rows.n_split_rows;
+                d->unit_nnz = unit_nnz;
+                d->has_rows = true;
+            }
+            if (!dev::device_validate(d->has_segment ? &seg : nullptr, d->has_rows ? &rows : nullptr, M, N, segw, st))
+                throw StatusError(VCSRMC_INTERNAL, "device-built format failed its index checks");
+            if (plans & (1 << VCSRMC_PLAN_BAND)) {
+                // The band view is built on the host from a copy of the CSR (values divided by the
+                // scale, as the row view holds them).
+                dev::RowViewHost rv;
+                rv.rp.resize(size_t(M) + 1);
+                rv.cols.resize(size_t(nnz));
+                rv.vals.resize(size_t(nnz));
+                cuda_check(cudaMemcpyAsync(rv.rp.data(), row_ptr, sizeof(int) * (size_t(M) + 1), cudaMemcpyDeviceToHost, st),
+                           "cudaMemcpyAsync");
+                if (nnz) {
+                    cuda_check(cudaMemcpyAsync(rv.cols.data(), col, sizeof(int) * size_t(nnz), cudaMemcpyDeviceToHost, st),
+                               "cudaMemcpyAsync");
+                    cuda_check(cudaMemcpyAsync(rv.vals.data(), val, sizeof(float) * size_t(nnz), cudaMemcpyDeviceToHost, st),
+                               "cudaMemcpyAsync");
+                }
+                cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+                const float inv_scale = 1.0f / scale;
+                for (float& x : rv.vals) x *= inv_scale;
+                int H = o.band_rows;
+                if (H == 0) H = dev::choose_band(rv, M).band_rows;
+                dev::BandViewHost bv = dev::build_band_view(rv, M, H, resolve_threads(0));
+                d->band_rows = bv.band_rows;
+                d->n_bands = int(bv.tile_ptr.size()) - 1;
+                d->n_tiles = int64_t(bv.tile_col.size());
+                d->tile_ptr = upload_array(bv.tile_ptr.data(), bv.tile_ptr.size(), st);
+                d->tile_col = upload_array(bv.tile_col.data(), bv.tile_col.size(), st);
+                d->tile_eptr = upload_array(bv.tile_eptr.data(), bv.tile_eptr.size(), st);
+                d->ents = upload_array(bv.ents.data(), bv.ents.size(), st);
+                cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+                d->has_band = true;
+            }
+            cuda_check(cudaMalloc(&d->status, sizeof(uint32_t)), "cudaMalloc");
+            cuda_check(cudaMemsetAsync(d->status, 0, sizeof(uint32_t), st), "cudaMemsetAsync");
+            cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        } catch (...) {
+            free_device(d);
+            throw;
+        }
+        *out = d;
+    });
+}
+
+VCSRMC_EXPORT int vcsrmc_device_download(const vcsrmc_device_format* d, vcsrmc_format** out) {
+    return guarded([&] {
+        if (!d || !out) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        if (!d->has_segment) throw StatusError(VCSRMC_INVALID_ARG, "the SEGMENT plan layout is not resident");
+        DeviceGuard guard(d->device);
+        const int64_t G = d->n_groups, S = d->n_slots, I = d->n_items;
+        std::vector<int4> gmeta(static_cast<size_t>(G));
+        std::vector<int2> items(static_cast<size_t>(I));
+        std::vector<int8_t> lcol(static_cast<size_t>(S));
+        auto* f = new vcsrmc_format;
+        try {
+            VCSRMC& v = f->v;
+            v.M = d->M;
+            v.N = d->N;
+            v.segw = d->segw;
+            v.bundle = 16;
+            v.num_segments = d->num_segments;
+            v.fp32 = d->fp32 != 0;
+            v.scale = d->scale;
+            v.group_rows.resize(size_t(G) * 16);
+            v.val.resize(size_t(S));
+            if (G) {
+                cuda_check(cudaMemcpy(gmeta.data(), d->gmeta, sizeof(int4) * size_t(G), cudaMemcpyDeviceToHost), "cudaMemcpy");
+                cuda_check(cudaMemcpy(v.group_rows.data(), d->grows, sizeof(int) * size_t(G) * 16, cudaMemcpyDeviceToHost),
+                           "cudaMemcpy");
+            }
+            if (I) cuda_check(cudaMemcpy(items.data(), d->items, sizeof(int2) * size_t(I), cudaMemcpyDeviceToHost), "cudaMemcpy");
+            if (S) {
+                cuda_check(cudaMemcpy(lcol.data(), d->lcol, size_t(S), cudaMemcpyDeviceToHost), "cudaMemcpy");
+                if (d->fp32) {
+                    cuda_check(cudaMemcpy(v.val.data(), d->val, sizeof(float) * size_t(S), cudaMemcpyDeviceToHost), "cudaMemcpy");
+                } else {
+                    std::vector<__half> h(static_cast<size_t>(S));
+                    cuda_check(cudaMemcpy(h.data(), d->val, sizeof(__half) * size_t(S), cudaMemcpyDeviceToHost), "cudaMemcpy");
+                    for (int64_t i = 0; i < S; ++i) v.val[size_t(i)] = __half2float(h[size_t(i)]);
+                }
+            }
+            v.group_ptr.resize(size_t(G) + 1);
+            v.group_depth.resize(size_t(G));
+            v.group_seg_base.resize(size_t(G));
+            for (int64_t g = 0; g < G; ++g) {
+                v.group_ptr[size_t(g)] = gmeta[size_t(g)].x;
+                v.group_depth[size_t(g)] = gmeta[size_t(g)].y;
+                v.group_seg_base[size_t(g)] = gmeta[size_t(g)].z;
+            }
+            v.group_ptr[size_t(G)] = int(S);
+            v.lcol.assign(lcol.begin(), lcol.end());
+            v.item_gbeg.resize(size_t(I));
+            v.item_gend.resize(size_t(I));
+            for (int64_t i = 0; i < I; ++i) {
+                v.item_gbeg[size_t(i)] = items[size_t(i)].x;
+                v.item_gend[size_t(i)] = items[size_t(i)].y;
+            }
+        } catch (...) {
+            delete f;
+            throw;
+        }
+        *out = f;
     });
 }

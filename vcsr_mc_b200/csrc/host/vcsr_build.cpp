@@ -31,14 +31,18 @@
 
 namespace vcsrmc {
 
-float half_scale(const CSR& csr) {
+float half_scale_from_absmax(float amax) {
     constexpr float kHalfHeadroom = 60000.0f;           // largest |a| kept after scaling
     constexpr float kHalfMinNormal = 6.103515625e-05f;  // smallest normal fp16
-    float amax = 0.0f;
-    for (float v : csr.val) amax = std::max(amax, std::fabs(v));
     if (amax > kHalfHeadroom) return amax / kHalfHeadroom;
     if (amax > 0.0f && amax < kHalfMinNormal) return amax / kHalfHeadroom;
     return 1.0f;
+}
+
+float half_scale(const CSR& csr) {
+    float amax = 0.0f;
+    for (float v : csr.val) amax = std::max(amax, std::fabs(v));
+    return half_scale_from_absmax(amax);
 }
 
 namespace {
