@@ -161,6 +161,10 @@ int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const vcsrmc_upload_o
 int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const int32_t* row_ptr, const int32_t* col,
                         const float* val, int fp32, int segw, int device,
                         const vcsrmc_upload_options* opts, void* stream, vcsrmc_device_format** out);
+/* half_scale (src/vcsr_mc.cu:14-22) of nnz fp32 values in device memory (current device),
+ * blocking. Allocates nothing: its scratch word is a file-scope device array, and concurrent
+ * calls in one process are serialised. */
+int vcsrmc_half_scale_device(const float* val, int64_t nnz, void* stream, float* scale);
 /* Copies the SEGMENT arrays of a device format back into a host format (values as the device
  * holds them: FP16 formats keep them rounded to fp16). */
 int vcsrmc_device_download(const vcsrmc_device_format* d, vcsrmc_format** out);

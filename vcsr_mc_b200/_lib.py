@@ -96,6 +96,7 @@ PROTOTYPES = {
     "vcsrmc_build_device": (_int, [_i32, _i32, _i64, _p, _p, _p, _int, _int, _int, ctypes.POINTER(UploadOptions), _p,
                                    _pp]),
     "vcsrmc_device_download": (_int, [_p, _pp]),
+    "vcsrmc_half_scale_device": (_int, [_p, _i64, _p, ctypes.POINTER(ctypes.c_float)]),
     "vcsrmc_device_info_get": (_int, [_p, ctypes.POINTER(DeviceInfo)]),
     "vcsrmc_device_free": (_int, [_p]),
     "vcsrmc_device_status": (_int, [_p, ctypes.POINTER(ctypes.c_uint32), _int]),

@@ -356,6 +356,23 @@ float device_abs_max(const float* val, int64_t nnz, cudaStream_t st) {
     return f;
 }
 
+// Scratch of device_abs_max_noalloc: one word per device for the whole library, so that call
+// allocates nothing (its callers serialise on it).
+static __device__ __align__(256) unsigned g_abs_max_scratch[1];
+
+float device_abs_max_noalloc(const float* val, int64_t nnz, cudaStream_t st) {
+    if (nnz <= 0) return 0.f;
+    void* scratch = nullptr;
+    check(cudaGetSymbolAddress(&scratch, g_abs_max_scratch), "cudaGetSymbolAddress");
+    check(cudaMemsetAsync(scratch, 0, sizeof(unsigned), st), "cudaMemsetAsync");
+    abs_max_kernel<<<blocks_for(nnz), 256, 0, st>>>(val, nnz, static_cast<unsigned*>(scratch));
+    check(cudaGetLastError(), "abs_max_kernel");
+    const unsigned bits = read_one(static_cast<const unsigned*>(scratch), st);
+    float f;
+    std::memcpy(&f, &bits, sizeof f);
+    return f;
+}
+
 bool device_csr_rows_sorted(const int* row_ptr, const int* col, int M, int N, int64_t nnz, cudaStream_t st) {
     Buf<int> bad(1);
     check(cudaMemsetAsync(bad.p, 0, sizeof(int), st), "cudaMemsetAsync");

@@ -33,6 +33,10 @@ struct RowsLayout {
 // Largest |val| (exact); the FP16 scale follows from it as in half_scale.
 float device_abs_max(const float* val, int64_t nnz, cudaStream_t st);
 
+// Same, without allocating: the scratch word is a file-scope device array (one per device), so
+// calls must not overlap (the C ABI serialises them).
+float device_abs_max_noalloc(const float* val, int64_t nnz, cudaStream_t st);
+
 // Checks row_ptr (0 first, non-decreasing, nnz last) and that every row's columns are strictly
 // ascending and inside [0, N). Returns false otherwise (blocking).
 bool device_csr_rows_sorted(const int* row_ptr, const int* col, int M, int N, int64_t nnz, cudaStream_t st);

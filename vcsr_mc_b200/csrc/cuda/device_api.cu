@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -692,5 +693,14 @@ VCSRMC_EXPORT int vcsrmc_device_download(const vcsrmc_device_format* d, vcsrmc_f
             throw;
         }
         *out = f;
+    });
+}
+
+VCSRMC_EXPORT int vcsrmc_half_scale_device(const float* val, int64_t nnz, void* stream, float* scale) {
+    return guarded([&] {
+        if (!scale || nnz < 0 || (nnz > 0 && !val)) throw StatusError(VCSRMC_INVALID_ARG, "bad arguments");
+        static std::mutex scratch_mu;  // one scratch word per device: calls do not overlap
+        std::lock_guard<std::mutex> lock(scratch_mu);
+        *scale = half_scale_from_absmax(dev::device_abs_max_noalloc(val, nnz, static_cast<cudaStream_t>(stream)));
     });
 }
