@@ -483,13 +483,24 @@ def main() -> None:
     # End to end through the C ABI with host buffers: every step uploads its B from pinned host
     # memory, runs the SpMM and downloads its C. Steps alternate between two device copies of B
     # and C so that the upload of step i+1 (copy stream 1) overlaps the download of step i (copy
-    # stream 2): PCIe moves both directions at once. Timed with events on the compute stream,
-    # max over ranks.
+    # stream 2): PCIe moves both directions at once. With several ranks each rank uploads 1/N of
+    # B's rows and the ranks all-gather the full B over NVLink (NCCL), instead of every rank
+    # pushing the whole B through its own PCIe link. Timed with events on the compute stream, max
+    # over ranks.
     e2e = None
     if not args.no_e2e and args.e2e_steps > 0:
-        hB = B.cpu().pin_memory()
+        if world > 1:
+            piece = (N + world - 1) // world
+            lo, hi = min(rank * piece, N), min((rank + 1) * piece, N)
+            hB = torch.zeros((piece, O_COLS), dtype=B.dtype).pin_memory()
+            hB[: hi - lo] = B[lo:hi].cpu()
+            Bfull = [torch.empty((world * piece, O_COLS), dtype=B.dtype, device="cuda") for _ in range(2)]
+            Bpiece = [torch.empty((piece, O_COLS), dtype=B.dtype, device="cuda") for _ in range(2)]
+            Bd = [t[:N] for t in Bfull]
+        else:
+            hB = B.cpu().pin_memory()
+            Bd = [B, torch.empty_like(B)]
         hC = torch.empty(C.shape, dtype=torch.float32).pin_memory()
-        Bd = [B, torch.empty_like(B)]
         Cd = [C, torch.empty_like(C)]
         up_stream, down_stream = torch.cuda.Stream(), torch.cuda.Stream()
         ev_up = [torch.cuda.Event() for _ in range(2)]
@@ -502,7 +513,11 @@ def main() -> None:
                 if i >= 2:  # buffer k was read by the SpMM of step i - 2
                     up_stream.wait_event(ev_comp[k])
                 with torch.cuda.stream(up_stream):
-                    Bd[k].copy_(hB, non_blocking=True)
+                    if world > 1:
+                        Bpiece[k].copy_(hB, non_blocking=True)
+                        dist.all_gather_into_tensor(Bfull[k], Bpiece[k])
+                    else:
+                        Bd[k].copy_(hB, non_blocking=True)
                     ev_up[k].record(up_stream)
                 stream.wait_event(ev_up[k])
                 if i >= 2:  # C buffer k was read by the download of step i - 2
@@ -533,7 +548,9 @@ def main() -> None:
         e2e = {"value": flops / (float(e2e_ms) * 1e-3) / 1e9, "unit": "GFLOP/s",
                "h2d_bytes_per_step": int(hB.numel() * hB.element_size()),
                "d2h_bytes_per_step": int(hC.numel() * hC.element_size()), "ms_per_step": float(e2e_ms),
-               "pipelining": "upload of step i+1 overlaps download of step i (two device buffers, two copy streams)"}
+               "pipelining": "upload of step i+1 overlaps download of step i (two device buffers, two copy streams)",
+               "b_staging": ("each rank uploads 1/N of B, NCCL all-gather over NVLink" if world > 1 else
+                             "B uploaded whole")}
         del Bd, Cd, hB, hC
 
     cusparse = None
