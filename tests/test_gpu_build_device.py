@@ -95,6 +95,16 @@ def test_spmm_on_device_built_format(cuda, name, plan, fp32):
     dV.free()
 
 
+@pytest.mark.parametrize("name", ["c1", "zipf", "rmat", "empty_rows"])
+def test_device_build_rows_units_match_host(cuda, name):
+    """The ROWS layout's work units follow the same packing whichever builder made the format."""
+    A = MATS[name]
+    a = device_build(cuda, A, False, 32, plans=[vm.PLAN_ROWS]).info()
+    b = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=False, segw=32), plans=[vm.PLAN_ROWS]).info()
+    for k in ("n_units", "rows_unit_nnz", "n_split_rows"):
+        assert a[k] == b[k], k
+
+
 def test_device_build_half_scale(cuda):
     rp, col, val = random_csr(64, 96, 0.1, seed=4, scale=1e6)
     A = vm.CSR.from_arrays(64, 96, rp, col, val)

@@ -18,8 +18,8 @@
 //   4. items: runs of at most chunk = max(1, min(32, G / 4096)) groups of one segment, then a
 //      stable radix sort by slot count, heaviest first.
 // The row view needs no reordering: a CSR row with ascending columns already lists its entries
-// in the format's order (ascending segment, then local column). Work units are packed inside
-// aligned blocks of 16 rows (heavy-row chunks first, as the host view does).
+// in the format's order (ascending segment, then local column). Its work units come from row_ptr
+// alone, packed on the host by the same rule as the host-built view (pack_units).
 #include <cub/cub.cuh>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -28,9 +28,11 @@
 #include <climits>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "../capi_internal.hpp"
 #include "build_device.hpp"
+#include "plan_rows.hpp"
 
 namespace vcsrmc {
 namespace dev {
@@ -240,52 +242,6 @@ __global__ void scale_values_kernel(const float* __restrict__ val, int64_t n, fl
         const float v = val[i] * inv_scale;
         if constexpr (kF32) static_cast<float*>(out)[i] = v;
         else static_cast<__half*>(out)[i] = __float2half_rn(v);
-    }
-}
-
-// Work units of a block of 16 rows: heavy rows (> u entries) as u-entry chunks, runs of light
-// rows with together <= u entries. Count pass (write = false) or write pass.
-template <bool kWrite>
-__global__ void units_kernel(const int* __restrict__ rp, int M, int u, int* __restrict__ n_heavy_units,
-                             int* __restrict__ n_light_units, int* __restrict__ n_split, const int* __restrict__ heavy_off,
-                             const int* __restrict__ light_off, const int* __restrict__ split_off, int64_t light_base,
-                             int4* __restrict__ units, int* __restrict__ split_rows) {
-    const int nb = (M + 15) / 16;
-    for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < nb; b += gridDim.x * blockDim.x) {
-        const int r0 = b * 16, r1 = min(M, r0 + 16);
-        int nh = 0, nl = 0, ns = 0;
-        int64_t hpos = kWrite ? heavy_off[b] : 0, lpos = kWrite ? light_base + light_off[b] : 0;
-        int spos = kWrite ? split_off[b] : 0;
-        for (int r = r0; r < r1; ++r) {
-            const int len = rp[r + 1] - rp[r];
-            if (len > u) {
-                if (kWrite) split_rows[spos++] = r;
-                ++ns;
-                for (int p = rp[r]; p < rp[r + 1]; p += u) {
-                    if (kWrite) units[hpos++] = make_int4(r, int(unsigned(r + 1) | 0x80000000u), p, min(rp[r + 1], p + u));
-                    ++nh;
-                }
-            }
-        }
-        int r = r0;
-        while (r < r1) {
-            if (rp[r + 1] - rp[r] > u) { ++r; continue; }
-            const int rb = r;
-            int n = 0;
-            while (r < r1) {
-                const int len = rp[r + 1] - rp[r];
-                if (len > u || (r > rb && n + len > u)) break;
-                n += len;
-                ++r;
-            }
-            if (kWrite) units[lpos++] = make_int4(rb, r, rp[rb], rp[r]);
-            ++nl;
-        }
-        if (!kWrite) {
-            n_heavy_units[b] = nh;
-            n_light_units[b] = nl;
-            n_split[b] = ns;
-        }
     }
 }
 
@@ -511,36 +467,31 @@ RowsLayout build_rows_layout(const int* row_ptr, const int* col, const float* va
         else scale_values_kernel<false><<<blocks_for(nnz), 256, 0, st>>>(val, nnz, 1.0f / scale, vals.p);
         check(cudaGetLastError(), "scale_values_kernel");
     }
-    const int nb = (M + 15) / 16;
-    Buf<int> nh(size_t(nb) + 1), nl(size_t(nb) + 1), ns(size_t(nb) + 1), ho(size_t(nb) + 1), lo(size_t(nb) + 1),
-        so(size_t(nb) + 1);
-    check(cudaMemsetAsync(nh.p + nb, 0, sizeof(int), st), "cudaMemsetAsync");
-    check(cudaMemsetAsync(nl.p + nb, 0, sizeof(int), st), "cudaMemsetAsync");
-    check(cudaMemsetAsync(ns.p + nb, 0, sizeof(int), st), "cudaMemsetAsync");
-    if (nb) {
-        units_kernel<false><<<blocks_for(nb), 256, 0, st>>>(rp.p, M, unit_nnz, nh.p, nl.p, ns.p, nullptr, nullptr,
-                                                            nullptr, 0, nullptr, nullptr);
-        check(cudaGetLastError(), "units_kernel");
-    }
-    exclusive_scan(nh.p, ho.p, int64_t(nb) + 1, st);
-    exclusive_scan(nl.p, lo.p, int64_t(nb) + 1, st);
-    exclusive_scan(ns.p, so.p, int64_t(nb) + 1, st);
-    const int64_t n_heavy = nb ? read_one(ho.p + nb, st) : 0;
-    const int64_t n_light = nb ? read_one(lo.p + nb, st) : 0;
-    const int64_t n_split = nb ? read_one(so.p + nb, st) : 0;
-    Buf<int4> units(static_cast<size_t>(n_heavy + n_light));
-    Buf<int> split(static_cast<size_t>(n_split));
-    if (nb) {
-        units_kernel<true><<<blocks_for(nb), 256, 0, st>>>(rp.p, M, unit_nnz, nullptr, nullptr, nullptr, ho.p, lo.p,
-                                                           so.p, n_heavy, units.p, split.p);
-        check(cudaGetLastError(), "units_kernel");
-    }
+    // Work units are packed on the host from row_ptr alone (M + 1 integers; the entries stay on
+    // the device) with the same greedy rule as the host-built row view.
+    std::vector<int> hrp(size_t(M) + 1);
+    check(cudaMemcpyAsync(hrp.data(), row_ptr, sizeof(int) * (size_t(M) + 1), cudaMemcpyDeviceToHost, st),
+          "cudaMemcpyAsync");
+    check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    std::vector<RowViewHost::Unit> hunits;
+    std::vector<int> hsplit;
+    pack_units(hrp.data(), M, unit_nnz, hunits, hsplit);
+    static_assert(sizeof(RowViewHost::Unit) == sizeof(int4), "unit layout");
+    Buf<int4> units(hunits.size());
+    Buf<int> split(hsplit.size());
+    if (!hunits.empty())
+        check(cudaMemcpyAsync(units.p, hunits.data(), sizeof(int4) * hunits.size(), cudaMemcpyHostToDevice, st),
+              "cudaMemcpyAsync");
+    if (!hsplit.empty())
+        check(cudaMemcpyAsync(split.p, hsplit.data(), sizeof(int) * hsplit.size(), cudaMemcpyHostToDevice, st),
+              "cudaMemcpyAsync");
+    const int64_t n_units = int64_t(hunits.size()), n_split = int64_t(hsplit.size());
     check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
     R.rp = rp.release();
     R.cols = cols.release();
     R.vals = vals.release();
     R.units = units.release();
-    R.n_units = n_heavy + n_light;
+    R.n_units = n_units;
     R.split_rows = split.release();
     R.n_split_rows = int(n_split);
     return R;

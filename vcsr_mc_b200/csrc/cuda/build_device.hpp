@@ -47,8 +47,8 @@ SegmentLayout build_segment_layout(const int* row_ptr, const int* col, const flo
                                    int segw, bool fp32, float scale, cudaStream_t st);
 
 // The row view: the CSR itself (rows sorted by column are already in the format's entry order),
-// values divided by the scale, and work units of at most unit_nnz entries packed inside aligned
-// blocks of 16 rows.
+// values divided by the scale, and the work units of the host-built view (packed on the host from
+// row_ptr).
 RowsLayout build_rows_layout(const int* row_ptr, const int* col, const float* val, int M, int64_t nnz, bool fp32,
                              float scale, int unit_nnz, cudaStream_t st);
 

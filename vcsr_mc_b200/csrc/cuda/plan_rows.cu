@@ -315,6 +315,34 @@ int choose_unit_nnz(int64_t nnz, int sms) {
     return u;
 }
 
+void pack_units(const int* rp, int M, int unit_nnz, std::vector<RowViewHost::Unit>& units,
+                std::vector<int>& split_rows) {
+    units.clear();
+    split_rows.clear();
+    // heavy-row chunks first, then runs of light rows
+    for (int r = 0; r < M; ++r) {
+        const int len = rp[r + 1] - rp[r];
+        if (len > unit_nnz) {
+            split_rows.push_back(r);
+            for (int p = rp[r]; p < rp[r + 1]; p += unit_nnz)
+                units.push_back({r, int((unsigned(r + 1)) | 0x80000000u), p, std::min(rp[r + 1], p + unit_nnz)});
+        }
+    }
+    int r = 0;
+    while (r < M) {
+        if (rp[r + 1] - rp[r] > unit_nnz) { ++r; continue; }
+        const int rb = r;
+        int n = 0;
+        while (r < M && r - rb < kUnitRows) {
+            const int len = rp[r + 1] - rp[r];
+            if (len > unit_nnz || (r > rb && n + len > unit_nnz)) break;
+            n += len;
+            ++r;
+        }
+        units.push_back({rb, r, rp[rb], rp[r]});
+    }
+}
+
 RowViewHost build_row_view(const VCSRMC& v, int unit_nnz) {
     RowViewHost h;
     const int M = v.M;
@@ -353,28 +381,7 @@ RowViewHost build_row_view(const VCSRMC& v, int unit_nnz) {
             }
         }
     }
-    // work units: heavy-row chunks first, then runs of light rows
-    for (int r = 0; r < M; ++r) {
-        const int len = h.rp[r + 1] - h.rp[r];
-        if (len > unit_nnz) {
-            h.split_rows.push_back(r);
-            for (int p = h.rp[r]; p < h.rp[r + 1]; p += unit_nnz)
-                h.units.push_back({r, int((unsigned(r + 1)) | 0x80000000u), p, std::min(h.rp[r + 1], p + unit_nnz)});
-        }
-    }
-    int r = 0;
-    while (r < M) {
-        if (h.rp[r + 1] - h.rp[r] > unit_nnz) { ++r; continue; }
-        const int rb = r;
-        int n = 0;
-        while (r < M && r - rb < kUnitRows) {
-            const int len = h.rp[r + 1] - h.rp[r];
-            if (len > unit_nnz || (r > rb && n + len > unit_nnz)) break;
-            n += len;
-            ++r;
-        }
-        h.units.push_back({rb, r, h.rp[rb], h.rp[r]});
-    }
+    pack_units(h.rp.data(), M, unit_nnz, h.units, h.split_rows);
     return h;
 }
 
