@@ -108,6 +108,11 @@ int vcsrmc_csr_view_get(const vcsrmc_csr* csr, vcsrmc_csr_view* out);
 /* Rows [r0, r1) as a CSR of their own (row ids rebased to 0). */
 int vcsrmc_csr_row_slice(const vcsrmc_csr* csr, int32_t r0, int32_t r1, vcsrmc_csr** out);
 void vcsrmc_csr_free(vcsrmc_csr* csr);
+/* Binary CSR cache: a 32-byte header ("VCSRMC1\0", int64 M, N, nnz), then row_ptr (int32,
+ * M + 1), col (int32, nnz), val (fp32, nnz), little-endian. Loading validates sizes, row_ptr
+ * and the column range (IO_ERR for an unreadable file, FORMAT_ERR for a malformed one). */
+int vcsrmc_csr_save(const vcsrmc_csr* csr, const char* path);
+int vcsrmc_csr_load(const char* path, vcsrmc_csr** out);
 
 /* ---- reordering: include/reorder.hpp:17-77 rcm_column_order, :82-108
  *      apply_column_permutation ---------------------------------------------------------- */

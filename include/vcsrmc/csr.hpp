@@ -51,4 +51,10 @@ VCSRMC_CXX_API CSR coo_to_csr(const COO& coo);
 // Rows [r0, r1) of `csr` as a CSR of their own (row ids rebased to 0; columns unchanged).
 VCSRMC_CXX_API CSR csr_row_slice(const CSR& csr, int r0, int r1);
 
+// Binary CSR cache (no reference counterpart): a 32-byte header ("VCSRMC1\0", int64 M, N, nnz)
+// followed by row_ptr (int32, M + 1), col (int32, nnz) and val (fp32, nnz), little-endian.
+// Loading checks the sizes, row_ptr (0 first, non-decreasing, nnz last) and the column range.
+VCSRMC_CXX_API void save_csr_binary(const CSR& csr, const std::string& path);
+VCSRMC_CXX_API CSR load_csr_binary(const std::string& path);
+
 }  // namespace vcsrmc

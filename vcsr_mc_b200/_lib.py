@@ -83,6 +83,8 @@ PROTOTYPES = {
     "vcsrmc_csr_view_get": (_int, [_p, ctypes.POINTER(CsrView)]),
     "vcsrmc_csr_row_slice": (_int, [_p, _i32, _i32, _pp]),
     "vcsrmc_csr_free": (None, [_p]),
+    "vcsrmc_csr_save": (_int, [_p, ctypes.c_char_p]),
+    "vcsrmc_csr_load": (_int, [ctypes.c_char_p, _pp]),
     "vcsrmc_rcm_column_order": (_int, [_p, _p]),
     "vcsrmc_apply_column_permutation": (_int, [_p, _p, _i32, _p]),
     "vcsrmc_half_scale": (_int, [_p, _pf32]),

@@ -80,6 +80,10 @@ class CSR:
         call("vcsrmc_csr_row_slice", self._h, r0, r1, ctypes.byref(h))
         return CSR(h)
 
+    def save(self, path: str) -> None:
+        """Binary cache of this CSR (vcsrmc_csr_save); load it with load_csr."""
+        call("vcsrmc_csr_save", self.handle, path.encode())
+
     @staticmethod
     def from_arrays(M: int, N: int, row_ptr, col, val) -> "CSR":
         rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
@@ -94,6 +98,13 @@ class CSR:
         h = ctypes.c_void_p()
         call("vcsrmc_gen_csr", kind, param, seed, nthreads, ctypes.byref(h))
         return CSR(h)
+
+
+def load_csr(path: str) -> CSR:
+    """A CSR saved by CSR.save (binary cache; vcsrmc_csr_load)."""
+    h = ctypes.c_void_p()
+    call("vcsrmc_csr_load", path.encode(), ctypes.byref(h))
+    return CSR(h)
 
 
 def read_matrix_market(path: str) -> CSR:

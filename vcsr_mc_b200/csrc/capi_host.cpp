@@ -58,6 +58,22 @@ VCSRMC_EXPORT int vcsrmc_csr_read_mtx(const char* path, vcsrmc_csr** out) {
     });
 }
 
+VCSRMC_EXPORT int vcsrmc_csr_save(const vcsrmc_csr* h, const char* path) {
+    return guarded([&] {
+        if (!h || !path) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        save_csr_binary(h->csr, path);
+    });
+}
+
+VCSRMC_EXPORT int vcsrmc_csr_load(const char* path, vcsrmc_csr** out) {
+    return guarded([&] {
+        if (!path || !out) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        auto* h = new vcsrmc_csr;
+        try { h->csr = load_csr_binary(path); } catch (...) { delete h; throw; }
+        *out = h;
+    });
+}
+
 VCSRMC_EXPORT int vcsrmc_csr_from_coo(int32_t M, int32_t N, int64_t nnz, const int32_t* rows,
                                       const int32_t* cols, const float* vals, vcsrmc_csr** out) {
     return guarded([&] {
