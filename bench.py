@@ -39,7 +39,9 @@ if ROOT not in sys.path:
 O_COLS = 128
 L2_BYTES = 126 * (1 << 20)
 SEED = 0
-CACHE_DIR = os.environ.get("VCSRMC_BENCH_CACHE", "/dev/shm/vcsrmc_bench")
+# Generated CSRs are cached inside the checkout (git- and gpurun-ignored) so that every rank of a
+# multi-GPU run, and later runs, load the same matrix instead of generating it again.
+CACHE_DIR = os.environ.get("VCSRMC_BENCH_CACHE", os.path.join(ROOT, ".bench_cache"))
 
 
 def log(msg: str) -> None:
