@@ -105,6 +105,20 @@ def test_rows_unit_sizes(cuda, unit_nnz, fp32, accumulate):
 
 
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
+@pytest.mark.parametrize("O", [1, 8, 16, 24, 32, 33, 48, 64, 65])
+@pytest.mark.parametrize("accumulate", [False, True], ids=["store", "accumulate"])
+def test_rows_narrow_widths(cuda, O, fp32, accumulate):
+    """ROWS plan on narrow B, where 2 or 4 entries share a lane group (rows split across folds and
+    steps, heavy-row chunks reduced into C)."""
+    A = vm.CSR.generate(vm.GEN_ZIPF, 1 << 14, seed=7)
+    B = np.random.default_rng(O).uniform(-1, 1, size=(A.N, O)).astype(np.float32)
+    base = np.random.default_rng(8).uniform(-1, 1, size=(A.M, O)).astype(np.float32) if accumulate else None
+    C, Bu = run_gpu(cuda, A, B, fp32, 32, 64, b_half=not fp32, accumulate_into=base, plan=vm.PLAN_ROWS,
+                    unit_nnz=32)
+    oracle_check(A, C, Bu, fp32, base=None if base is None else base.astype(np.float64))
+
+
+@pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
 @pytest.mark.parametrize("plan", PLANS, ids=PLAN_IDS)
 def test_stencil27(cuda, plan, fp32):
     A = vm.CSR.generate(vm.GEN_STENCIL27, 24, seed=0)

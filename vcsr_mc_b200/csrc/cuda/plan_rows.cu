@@ -249,6 +249,135 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     if (partial) write_lane<kE, kVec, RowOut::kReduce>(C + int64_t(rb) * ldc + c0, acc, scale, nv);
 }
 
+// The same plan for narrow B (O <= 64 fp16 or O <= 32 fp32 columns... in general O <= kL * kE / 2):
+// a row slice of B then needs only kW = kL / kF lanes, so each lane group works on kF entries at
+// once. Fold f of the group (lanes f * kW .. f * kW + kW - 1) takes entries f, f + kF, f + 2 kF, ...
+// of every staged batch. Per step of kF consecutive entries the folds' contributions to the same
+// row are summed across folds with shuffles (rows are non-decreasing along the entries, so the
+// folds sharing a row are contiguous); a row that continues past a step is carried in every
+// lane's accumulator; the fold holding a row's last entry writes the row.
+template <int kF, bool kVec, bool kAccumulate, typename VT, typename BT>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    vcsr_rows_folded_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
+                            const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
+                            int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale) {
+    constexpr int kE = Lane16<BT>::kElems;
+    constexpr int kL = Lane16<BT>::kLanes;
+    constexpr int kW = kL / kF;        // lanes per entry
+    constexpr int kSteps = kL / kF;    // steps per staged batch of kL entries
+    constexpr int kR = kSteps < kInFlight ? kSteps : kInFlight;
+    constexpr int kGroups = 32 / kL;
+    constexpr RowOut kOut = kAccumulate ? RowOut::kAdd : RowOut::kStore;
+    static_assert(kF == 2 || kF == 4, "fold of 2 or 4 entries");
+    __shared__ int2 stage_all[kWarpsPerBlock * 32];
+    const int lane = threadIdx.x & 31;
+    const int sub = lane / kL, sl = lane % kL;
+    const int fold = sl / kW, cl = sl % kW;
+    const unsigned gmask = kL == 32 ? kFull : (0xffffu << (16 * sub));
+    int2* stage = stage_all + (threadIdx.x >> 5) * 32 + sub * kL;
+    const int64_t unit = (int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5)) * kGroups + sub;
+    if (unit >= n_units) return;  // the whole group leaves together
+    const int4 u = units[unit];
+    const int c0 = kE * cl;  // one slab: O <= kW * kE
+    const int nv = max(0, min(kE, O - c0));
+    const char* bbase = reinterpret_cast<const char*>(B) + size_t(c0) * sizeof(BT);
+    const bool partial = (u.y & 0x80000000) != 0;
+    const int rb = u.x, pb = u.z, pe = u.w;
+    const int nrows = partial ? 1 : (u.y & 0x7fffffff) - rb;
+
+    const int my_end = (!partial && sl < nrows) ? rp[rb + sl + 1] : 0x7fffffff;
+    if (!partial && !kAccumulate) {
+        const int prev_end = __shfl_up_sync(gmask, my_end, 1, kL);
+        const int my_start = sl == 0 ? pb : prev_end;
+        unsigned empty = __ballot_sync(gmask, sl < nrows && my_start == my_end);
+        if (kL == 16) empty = (empty >> (16 * sub)) & 0xffffu;
+        const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        while (empty) {
+            const int i = __ffs(empty) - 1;
+            empty &= empty - 1;
+            if (fold == 0) write_lane<kE, kVec, RowOut::kStore>(C + int64_t(rb + i) * ldc + c0, zero, 1.f, nv);
+        }
+    }
+
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // the open row's sum (same in every fold)
+    int open_row = -1;
+    int mc = 0;
+    uint32_t mv = 0;
+    if (pb + sl < pe) {
+        mc = __ldcs(cols + pb + sl);
+        mv = a_bits<VT, BT>(vals + pb + sl);
+    }
+    for (int q = pb; q < pe; q += kL) {
+        const int n = min(kL, pe - q);
+        stage[sl] = make_int2(mc, int(mv));
+        mc = 0;
+        mv = 0;
+        if (q + kL + sl < pe) {
+            mc = __ldcs(cols + q + kL + sl);
+            mv = a_bits<VT, BT>(vals + q + kL + sl);
+        }
+        int lo = 0;
+        unsigned ends = 0;
+        if (!partial) {
+            const int e = q + sl;
+#pragma unroll
+            for (int step = kUnitRows / 2; step >= 1; step >>= 1) {
+                const int probe = __shfl_sync(gmask, my_end, (lo + step - 1) & (kL - 1), kL);
+                if (probe <= e) lo += step;
+            }
+            const int row_end = __shfl_sync(gmask, my_end, lo & (kL - 1), kL);
+            ends = __ballot_sync(gmask, sl < n && e + 1 == row_end);
+            if (kL == 16) ends = (ends >> (16 * sub)) & 0xffffu;
+        }
+        __syncwarp(gmask);
+        for (int t0 = 0; t0 < kSteps; t0 += kR) {
+            uint4 raw[kR];
+            uint32_t av[kR];
+#pragma unroll
+            for (int k = 0; k < kR; ++k) {
+                const int2 e = stage[(t0 + k) * kF + fold];
+                av[k] = uint32_t(e.y);
+                raw[k] = load16<kVec>(reinterpret_cast<const BT*>(bbase + int64_t(e.x) * row_bytes), nv);
+            }
+#pragma unroll
+            for (int k = 0; k < kR; ++k) {
+                const int j0 = (t0 + k) * kF;  // first entry of this step
+                int row[kF];
+#pragma unroll
+                for (int g = 0; g < kF; ++g) row[g] = __shfl_sync(gmask, lo, j0 + g, kL);
+                float c[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                fma_lane<VT, BT>(c, av[k], raw[k]);
+                float v[8];
+                const bool carry_in = row[fold] == open_row;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = c[i] + (carry_in ? acc[i] : 0.f);
+#pragma unroll
+                for (int d = 1; d < kF; ++d) {
+                    const bool same = fold >= d && row[fold - d] == row[fold];
+#pragma unroll
+                    for (int i = 0; i < kE; ++i) {
+                        const float o = __shfl_up_sync(gmask, c[i], d * kW, kL);
+                        if (same) v[i] += o;
+                    }
+                }
+                if ((ends >> (j0 + fold)) & 1u)
+                    write_lane<kE, kVec, kOut>(C + int64_t(rb + row[fold]) * ldc + c0, v, scale, nv);
+                if ((ends >> (j0 + kF - 1)) & 1u) {
+                    open_row = -1;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+                } else {
+                    open_row = row[kF - 1];
+#pragma unroll
+                    for (int i = 0; i < kE; ++i) acc[i] = __shfl_sync(gmask, v[i], (kF - 1) * kW + cl, kL);
+                }
+            }
+        }
+        __syncwarp(gmask);
+    }
+    if (partial && fold == 0) write_lane<kE, kVec, RowOut::kReduce>(C + int64_t(rb) * ldc + c0, acc, scale, nv);
+}
+
 // Zeroes C's heavy rows (the ones built from several reduced chunks) before an overwrite.
 __global__ void zero_rows_kernel(const int* __restrict__ rows, int n_rows, int O, float* __restrict__ C, int64_t ldc) {
     const int i = blockIdx.x;
@@ -260,14 +389,27 @@ __global__ void zero_rows_kernel(const int* __restrict__ rows, int n_rows, int O
 template <bool kVec, bool kAcc, typename VT, typename BT>
 cudaError_t launch_rows_t(const RowPlanView& P, const BT* B, int64_t ldb, int O, float* C, int64_t ldc,
                           cudaStream_t st) {
-    constexpr int kGroupsPerWarp = 32 / Lane16<BT>::kLanes;
+    constexpr int kL = Lane16<BT>::kLanes, kE = Lane16<BT>::kElems;
+    constexpr int kGroupsPerWarp = 32 / kL;
     const int64_t per_block = int64_t(kWarpsPerBlock) * kGroupsPerWarp;
     const int64_t blocks = (P.n_units + per_block - 1) / per_block;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+    const int row_bytes = int(ldb * int64_t(sizeof(BT)));
+    const VT* vals = static_cast<const VT*>(P.vals);
+    // narrow B: fold 4 or 2 entries into one lane group when a row slice fits a quarter or half
+    if (O <= kL * kE / 4) {
+        vcsr_rows_folded_kernel<4, kVec, kAcc, VT, BT><<<unsigned(blocks), kWarpsPerBlock * 32, 0, st>>>(
+            P.units, P.n_units, P.rp, P.cols, vals, B, row_bytes, O, C, ldc, P.scale);
+        return cudaGetLastError();
+    }
+    if (O <= kL * kE / 2) {
+        vcsr_rows_folded_kernel<2, kVec, kAcc, VT, BT><<<unsigned(blocks), kWarpsPerBlock * 32, 0, st>>>(
+            P.units, P.n_units, P.rp, P.cols, vals, B, row_bytes, O, C, ldc, P.scale);
+        return cudaGetLastError();
+    }
     const dim3 grid(unsigned(blocks), unsigned((O + 127) / 128));
     vcsr_rows_kernel<kVec, kAcc, VT, BT><<<grid, kWarpsPerBlock * 32, 0, st>>>(
-        P.units, P.n_units, P.rp, P.cols, static_cast<const VT*>(P.vals), B, int(ldb * int64_t(sizeof(BT))), O, C, ldc,
-        P.scale);
+        P.units, P.n_units, P.rp, P.cols, vals, B, row_bytes, O, C, ldc, P.scale);
     return cudaGetLastError();
 }
 
