@@ -68,7 +68,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---- TMA ---------------------------------------------------------------------------------
-// 2-D tiled bulk tensor load global -> shared (no multicast), completion on `bar`.
+// 2-D tiled bulk tensor load global -> this CTA's shared memory, completion on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
