@@ -303,6 +303,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
+    ap.add_argument("--no-c-gather", action="store_true", help="skip the separately timed gather of C to rank 0 (N > 1)")
     ap.add_argument("--cpu-sample-nnz", type=int, default=8_000_000)
     ap.add_argument("--build", choices=["host", "device"], default="host",
                     help="format construction: host (bit-identical to the reference builder) or device (GPU)")
@@ -555,6 +556,40 @@ def main() -> None:
                              "B uploaded whole")}
         del Bd, Cd, hB, hC
 
+    # Optional gather of C to rank 0 over NVLink (NCCL point-to-point), timed on its own: the
+    # SpMM needs no collective, so this is not part of the step.
+    c_gather = None
+    if dist is not None and not args.no_c_gather:
+        Cfull = torch.empty((M, O_COLS), dtype=torch.float32, device="cuda") if rank == 0 else None
+
+        def gather() -> None:
+            if rank == 0:
+                Cfull[r0:r1].copy_(C[:Ms])
+                ops = [dist.P2POp(dist.irecv, Cfull[int(cuts[k]):int(cuts[k + 1])], k) for k in range(1, world)
+                       if cuts[k + 1] > cuts[k]]
+            else:
+                ops = [dist.P2POp(dist.isend, C[:Ms], 0)] if Ms > 0 else []
+            for q in (dist.batch_isend_irecv(ops) if ops else []):  # empty shards send nothing
+                q.wait()
+
+        gather()  # the first point-to-point exchange also sets up NCCL's connections: untimed
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        gather()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gms = torch.tensor([g0.elapsed_time(g1)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(gms, op=dist.ReduceOp.MAX)
+        moved = (M - (r1 - r0 if rank == 0 else 0)) * O_COLS * 4
+        c_gather = {"ms": float(gms), "bytes_to_rank0": int(moved),
+                    "GB_per_s": moved / (float(gms) * 1e-3) / 1e9 if float(gms) > 0 else None,
+                    "how": "NCCL batch_isend_irecv into one M x O buffer on rank 0, max over ranks"}
+        del Cfull
+        barrier()
+
     cusparse = None
     if rank == 0 and not args.no_cusparse:
         cusparse = time_cusparse(rp, col, val, r0, r1, p0, p1, N, B, fp16, stream)
@@ -582,7 +617,8 @@ def main() -> None:
                                     "segment": "vcsr_mc_fp16_tc_kernel" if fp16 else "vcsr_mc_fp32_kernel"}[args.plan],
                          "kernel_ms": kern_ms, "kernel_ms_max_over_ranks": kern_max_ms,
                          "algorithmic_bytes": bytes_alg},
-            "cpu_baseline": cpu, "e2e": e2e, "cusparse": cusparse, "gpu_launches": args.steps * launches_per_step,
+            "cpu_baseline": cpu, "e2e": e2e, "cusparse": cusparse, "c_gather": c_gather,
+            "gpu_launches": args.steps * launches_per_step,
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "detail": {"nnz": nnz_total, "M": M, "N": N, "rank0_rows": Ms, "rank0_distinct_cols": D,
                        "groups": groups, "slots": slots, "items": items, "device_status": status,
