@@ -68,6 +68,9 @@ namespace {
 
 void cuda_check(cudaError_t e, const char* what) {
     if (e == cudaSuccess) return;
+    // A failed call also leaves its error as the thread's last runtime error, which the next
+    // launch check (cudaGetLastError) would report again; clear it (a sticky error stays).
+    cudaGetLastError();
     const int s = e == cudaErrorMemoryAllocation ? VCSRMC_OOM : VCSRMC_CUDA_ERR;
     throw StatusError(s, std::string(what) + ": " + cudaGetErrorString(e));
 }
