@@ -159,7 +159,8 @@ int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const vcsrmc_upload_o
 /* Device-side construction: builds the format of a CSR already in device memory (row_ptr[M+1],
  * col[nnz], val[nnz] on `device`; row_ptr from 0 to nnz, rows with strictly ascending columns)
  * and makes its plan layouts resident there, without a host copy of the matrix. opts may be NULL;
- * plans 0 = SEGMENT and ROWS (a BAND layout, when asked for, is built on the host from a copy).
+ * plans 0 = SEGMENT and ROWS, plus BAND on the same rule as vcsrmc_upload_ex; the BAND view is
+ * the one an upload of the same matrix makes (same band height, tiles and entry order).
  * Rows with equal per-segment entry counts are ordered by ascending row, so group_rows, lcol and
  * val can differ from vcsrmc_build_host's by a permutation inside such runs (the reference takes
  * that order from its hash map); every other array is identical. Blocking. */

@@ -105,6 +105,52 @@ def test_device_build_rows_units_match_host(cuda, name):
         assert a[k] == b[k], k
 
 
+BAND_CASES = [("c1", 0), ("zipf", 0), ("stencil", 0), ("stencil", 37), ("stencil", 1), ("rmat", 64),
+              ("rmat", 0), ("empty_rows", 0), ("empty_rows", 128)]
+
+
+@pytest.mark.parametrize("name,H", BAND_CASES, ids=[f"{n}-H{h}" for n, h in BAND_CASES])
+def test_device_band_view_equals_host(cuda, name, H):
+    """The BAND view built on the device (segmented sort, one warp per band cutting the greedy
+    tiles) is the host-built view: same band height (chosen from the same sampled bands when H is
+    0), same band and tile counts, and bit-identical SpMM results, which needs the same tiles with
+    their entries in the same order."""
+    torch = cuda
+    A = MATS[name]
+    a = device_build(torch, A, False, 32, plans=[vm.PLAN_BAND], band_rows=H)
+    b = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=False, segw=32), plans=[vm.PLAN_BAND], band_rows=H)
+    ia, ib = a.info(), b.info()
+    for k in ("band_rows", "n_bands", "n_tiles"):
+        assert ia[k] == ib[k], k
+    assert a.scale == b.scale
+    B = torch.from_numpy(vm.gen_dense_host(A.N, 96, seed=5)).cuda().half()
+    Ca = torch.full((A.M, 96), float("nan"), device="cuda")
+    Cb = torch.full((A.M, 96), float("nan"), device="cuda")
+    vm.spmm(a, B, Ca, accumulate=False, plan=vm.PLAN_BAND)
+    vm.spmm(b, B, Cb, accumulate=False, plan=vm.PLAN_BAND)
+    torch.cuda.synchronize()
+    assert a.status() == 0 and b.status() == 0
+    assert torch.equal(Ca, Cb)
+    rp, col, val = A.arrays()
+    ref, ab = ob.spmm_fp64(rp, col, val, B.float().cpu().numpy(), with_abs=True)
+    check_fp16(Ca.cpu().numpy(), ref, ab)
+    a.free()
+    b.free()
+
+
+@pytest.mark.parametrize("name", ["stencil", "zipf", "c1"])
+def test_device_build_default_plans_follow_upload(cuda, name):
+    """With the default plans the device builder adds BAND exactly where an upload does."""
+    A = MATS[name]
+    a = device_build(cuda, A, False, 32).info()
+    b = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=False, segw=32)).info()
+    assert a["plans"] == b["plans"]
+    assert (vm.PLAN_BAND in a["plans"]) == (name == "stencil")
+    if vm.PLAN_BAND in a["plans"]:
+        assert a["band_rows"] == b["band_rows"] and a["n_tiles"] == b["n_tiles"]
+    assert vm.PLAN_BAND not in device_build(cuda, A, True, 32).info()["plans"]
+
+
 def test_device_build_half_scale(cuda):
     rp, col, val = random_csr(64, 96, 0.1, seed=4, scale=1e6)
     A = vm.CSR.from_arrays(64, 96, rp, col, val)

@@ -19,7 +19,8 @@
 //      stable radix sort by slot count, heaviest first.
 // The row view needs no reordering: a CSR row with ascending columns already lists its entries
 // in the format's order (ascending segment, then local column). Its work units come from row_ptr
-// alone, packed on the host by the same rule as the host-built view (pack_units).
+// alone, packed on the host by the same rule as the host-built view (pack_units). The BAND view
+// (build_band_layout) sorts each band's entries by column and cuts its tiles with one warp per band.
 #include <cub/cub.cuh>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -292,6 +293,93 @@ __global__ void validate_rows_kernel(const int* __restrict__ rp, const int* __re
     }
 }
 
+// ---- BAND view ----------------------------------------------------------------------------------
+
+__global__ void gather_int_kernel(const int* __restrict__ src, const int* __restrict__ idx, int n, int* __restrict__ out) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = src[idx[i]];
+}
+
+// Band b's entries are [row_ptr[b * H], row_ptr[min(M, (b + 1) * H)]).
+__global__ void band_offsets_kernel(const int* __restrict__ rp, int M, int H, int nb, int* __restrict__ boff) {
+    for (int b = blockIdx.x * blockDim.x + threadIdx.x; b <= nb; b += gridDim.x * blockDim.x)
+        boff[b] = rp[int64_t(b) * H < M ? int64_t(b) * H : int64_t(M)];
+}
+
+// An entry's view word without its local column: row within the band (bits 5-11) and the fp16 bits
+// of value / scale (bits 16-31). One warp per row.
+__global__ void band_payload_kernel(const int* __restrict__ rp, const float* __restrict__ val, int M, int H,
+                                    float inv_scale, uint32_t* __restrict__ payload) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = int64_t(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < M; r += nwarps) {
+        const uint32_t row = uint32_t(r % H) << 5;
+        for (int p = rp[r] + lane; p < rp[r + 1]; p += 32)
+            payload[p] = row | (uint32_t(__half_as_ushort(__float2half_rn(val[p] * inv_scale))) << 16);
+    }
+}
+
+// Greedy 32-column tiles over a band's entries sorted by column: a tile starts at the first
+// column at or past the end of the previous tile. One warp per band walks its entries 32 at a
+// time; inside a chunk, the next start is the first lane (ballot) whose column reaches the current
+// end, repeated while one does. kWrite = false counts the tiles; kWrite = true writes tile_col,
+// tile_eptr and each entry's local column into ents.
+template <bool kWrite>
+__global__ void band_tiles_kernel(const int* __restrict__ boff, const int* __restrict__ scol, int nb,
+                                  int* __restrict__ ntiles, const int* __restrict__ tile_ptr,
+                                  int* __restrict__ tile_col, int* __restrict__ tile_eptr, uint32_t* __restrict__ ents) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = int64_t(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; b < nb; b += nwarps) {
+        const int e0 = boff[b], e1 = boff[b + 1];
+        int t = kWrite ? tile_ptr[b] : 0;
+        int64_t end = -1;  // first column past the current tile
+        int start = 0;     // the current tile's first column
+        for (int base = e0; base < e1; base += 32) {
+            const int i = base + lane;
+            const bool valid = i < e1;
+            const int c = valid ? scol[i] : 0;
+            int mine = start;  // the start of the tile this lane's entry falls in
+            unsigned pend = __ballot_sync(0xffffffffu, valid && c >= end);
+            while (pend) {
+                const int L = __ffs(pend) - 1;
+                const int s = __shfl_sync(0xffffffffu, c, L);
+                if (kWrite && lane == 0) {
+                    tile_col[t] = s;
+                    tile_eptr[t] = base + L;
+                }
+                ++t;
+                if (lane >= L) mine = s;
+                start = s;
+                end = int64_t(s) + 32;
+                pend = __ballot_sync(0xffffffffu, valid && c >= end);
+            }
+            if (kWrite && valid) ents[i] |= uint32_t(c - mine);
+        }
+        if (!kWrite && lane == 0) ntiles[b] = t;
+    }
+}
+
+// The checks build_band_view makes on the host: per band, tiles in range, covering exactly the
+// band's entries, each non-empty, starts ascending by at least 32 columns.
+__global__ void validate_band_kernel(const int* __restrict__ boff, const int* __restrict__ tile_ptr,
+                                     const int* __restrict__ tile_col, const int* __restrict__ tile_eptr, int nb,
+                                     int64_t T, int* bad) {
+    for (int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; b < nb; b += int64_t(gridDim.x) * blockDim.x) {
+        const int t0 = tile_ptr[b], t1 = tile_ptr[b + 1];
+        const int e0 = boff[b], e1 = boff[b + 1];
+        if (t0 < 0 || t1 < t0 || t1 > T) {
+            atomicOr(bad, 1);
+            continue;
+        }
+        if ((t1 > t0 && (tile_eptr[t0] != e0 || tile_eptr[t1] != e1)) || (t1 == t0 && e1 != e0)) atomicOr(bad, 2);
+        for (int t = t0; t < t1; ++t) {
+            if (tile_eptr[t + 1] <= tile_eptr[t] || tile_col[t] < 0 ||
+                (t > t0 && int64_t(tile_col[t]) < int64_t(tile_col[t - 1]) + 32))
+                atomicOr(bad, 4);
+        }
+    }
+}
+
 template <class T>
 void exclusive_scan(const T* in, T* out, int64_t n, cudaStream_t st) {
     if (n <= 0) return;
@@ -498,6 +586,115 @@ RowsLayout build_rows_layout(const int* row_ptr, const int* col, const float* va
     R.split_rows = split.release();
     R.n_split_rows = int(n_split);
     return R;
+}
+
+BandChoice choose_band_device(const int* row_ptr, const int* col, int M, cudaStream_t st) {
+    // The sampled ranges of all candidate heights overlap (every height samples row 0): the union
+    // of their rows is copied once, as merged intervals.
+    std::vector<int> store, bound;
+    return choose_band_sampled(M, [&](const std::vector<std::pair<int, int>>& ranges, std::vector<const int*>& first,
+                                      std::vector<const int*>& last) {
+        const size_t n = ranges.size();
+        std::vector<size_t> order(n);
+        for (size_t i = 0; i < n; ++i) order[i] = i;
+        std::sort(order.begin(), order.end(), [&](size_t a, size_t b) { return ranges[a] < ranges[b]; });
+        std::vector<std::pair<int, int>> merged;
+        std::vector<size_t> owner(n);
+        for (const size_t i : order) {
+            if (merged.empty() || ranges[i].first > merged.back().second) merged.push_back(ranges[i]);
+            else merged.back().second = std::max(merged.back().second, ranges[i].second);
+            owner[i] = merged.size() - 1;
+        }
+        // row_ptr at every range's ends and every interval's ends
+        std::vector<int> rows;
+        for (const auto& r : ranges) rows.insert(rows.end(), {r.first, r.second});
+        for (const auto& m : merged) rows.insert(rows.end(), {m.first, m.second});
+        const int nr = int(rows.size());
+        Buf<int> drows(rows.size()), dvals(rows.size());
+        check(cudaMemcpyAsync(drows.p, rows.data(), sizeof(int) * rows.size(), cudaMemcpyHostToDevice, st),
+              "cudaMemcpyAsync");
+        gather_int_kernel<<<blocks_for(nr), 256, 0, st>>>(row_ptr, drows.p, nr, dvals.p);
+        check(cudaGetLastError(), "gather_int_kernel");
+        bound.resize(rows.size());
+        check(cudaMemcpyAsync(bound.data(), dvals.p, sizeof(int) * rows.size(), cudaMemcpyDeviceToHost, st),
+              "cudaMemcpyAsync");
+        check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        const int* mb = bound.data() + 2 * n;
+        std::vector<int64_t> moff(merged.size() + 1, 0);
+        for (size_t m = 0; m < merged.size(); ++m) moff[m + 1] = moff[m] + (mb[2 * m + 1] - mb[2 * m]);
+        store.resize(size_t(moff.back()));
+        for (size_t m = 0; m < merged.size(); ++m)
+            if (moff[m + 1] > moff[m])
+                check(cudaMemcpyAsync(store.data() + moff[m], col + mb[2 * m], sizeof(int) * size_t(moff[m + 1] - moff[m]),
+                                      cudaMemcpyDeviceToHost, st),
+                      "cudaMemcpyAsync");
+        check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        for (size_t i = 0; i < n; ++i) {
+            const size_t m = owner[i];
+            first[i] = store.data() + moff[m] + (bound[2 * i] - mb[2 * m]);
+            last[i] = first[i] + (bound[2 * i + 1] - bound[2 * i]);
+        }
+    });
+}
+
+BandLayout build_band_layout(const int* row_ptr, const int* col, const float* val, int M, int64_t nnz, float scale,
+                             int band_rows, cudaStream_t st) {
+    if (band_rows < 1 || band_rows > kBandRows) throw StatusError(VCSRMC_INTERNAL, "band height out of range");
+    const int H = band_rows;
+    const int nb = int((int64_t(M) + H - 1) / H);
+    Buf<int> boff(size_t(nb) + 1), ntiles(size_t(nb) + 1), tile_ptr(size_t(nb) + 1);
+    band_offsets_kernel<<<blocks_for(int64_t(nb) + 1), 256, 0, st>>>(row_ptr, M, H, nb, boff.p);
+    check(cudaGetLastError(), "band_offsets_kernel");
+    Buf<int> scol(static_cast<size_t>(nnz));
+    Buf<uint32_t> ents(static_cast<size_t>(nnz));
+    if (nnz) {
+        Buf<uint32_t> payload(static_cast<size_t>(nnz));
+        band_payload_kernel<<<blocks_for(int64_t(M) * 32), 256, 0, st>>>(row_ptr, val, M, H, 1.0f / scale, payload.p);
+        check(cudaGetLastError(), "band_payload_kernel");
+        // Rows enter a band in ascending order, so a stable sort by column gives (column, row).
+        size_t tmp = 0;
+        check(cub::DeviceSegmentedSort::StableSortPairs(nullptr, tmp, col, scol.p, payload.p, ents.p, int(nnz), nb,
+                                                         boff.p, boff.p + 1, st),
+              "cub segmented sort");
+        Buf<uint8_t> t(tmp);
+        check(cub::DeviceSegmentedSort::StableSortPairs(t.p, tmp, col, scol.p, payload.p, ents.p, int(nnz), nb, boff.p,
+                                                         boff.p + 1, st),
+              "cub segmented sort");
+        check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    }
+    check(cudaMemsetAsync(ntiles.p, 0, sizeof(int) * (size_t(nb) + 1), st), "cudaMemsetAsync");
+    if (nb > 0) {
+        band_tiles_kernel<false><<<blocks_for(int64_t(nb) * 32), 256, 0, st>>>(boff.p, scol.p, nb, ntiles.p, nullptr,
+                                                                            nullptr, nullptr, nullptr);
+        check(cudaGetLastError(), "band_tiles_kernel");
+    }
+    exclusive_scan(ntiles.p, tile_ptr.p, int64_t(nb) + 1, st);
+    const int64_t T = read_one(tile_ptr.p + nb, st);
+    if (T < 0 || T > nnz) throw StatusError(VCSRMC_INTERNAL, "band view construction is inconsistent");
+    Buf<int> tile_col(static_cast<size_t>(T)), tile_eptr(size_t(T) + 1);
+    const int nnz32 = int(nnz);
+    check(cudaMemcpyAsync(tile_eptr.p + T, &nnz32, sizeof(int), cudaMemcpyHostToDevice, st), "cudaMemcpyAsync");
+    if (nb > 0) {
+        band_tiles_kernel<true><<<blocks_for(int64_t(nb) * 32), 256, 0, st>>>(boff.p, scol.p, nb, nullptr, tile_ptr.p,
+                                                                           tile_col.p, tile_eptr.p, ents.p);
+        check(cudaGetLastError(), "band_tiles_kernel");
+    }
+    Buf<int> bad(1);
+    check(cudaMemsetAsync(bad.p, 0, sizeof(int), st), "cudaMemsetAsync");
+    if (nb > 0) {
+        validate_band_kernel<<<blocks_for(nb), 256, 0, st>>>(boff.p, tile_ptr.p, tile_col.p, tile_eptr.p, nb, T, bad.p);
+        check(cudaGetLastError(), "validate_band_kernel");
+    }
+    if (read_one(bad.p, st) != 0) throw StatusError(VCSRMC_INTERNAL, "band view construction is inconsistent");
+    BandLayout L;
+    L.band_rows = H;
+    L.n_bands = nb;
+    L.n_tiles = T;
+    L.tile_ptr = tile_ptr.release();
+    L.tile_col = tile_col.release();
+    L.tile_eptr = tile_eptr.release();
+    L.ents = ents.release();
+    return L;
 }
 
 bool device_validate(const SegmentLayout* seg, const RowsLayout* rows, int M, int N, int segw, cudaStream_t st) {

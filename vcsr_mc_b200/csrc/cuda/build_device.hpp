@@ -5,6 +5,8 @@
 
 #include <cstdint>
 
+#include "plan_band.hpp"
+
 namespace vcsrmc {
 namespace dev {
 
@@ -30,6 +32,17 @@ struct RowsLayout {
     int n_split_rows = 0;
 };
 
+// Device arrays of the BAND plan, in the host-built view's layout (plan_band.hpp; the caller
+// owns them).
+struct BandLayout {
+    int* tile_ptr = nullptr;   // n_bands + 1
+    int* tile_col = nullptr;   // n_tiles
+    int* tile_eptr = nullptr;  // n_tiles + 1
+    uint32_t* ents = nullptr;  // nnz
+    int band_rows = 0, n_bands = 0;
+    int64_t n_tiles = 0;
+};
+
 // Largest |val| (exact); the FP16 scale follows from it as in half_scale.
 float device_abs_max(const float* val, int64_t nnz, cudaStream_t st);
 
@@ -51,6 +64,16 @@ SegmentLayout build_segment_layout(const int* row_ptr, const int* col, const flo
 // row_ptr).
 RowsLayout build_rows_layout(const int* row_ptr, const int* col, const float* val, int M, int64_t nnz, bool fp32,
                              float scale, int unit_nnz, cudaStream_t st);
+
+// The band height and entries per tile that choose_band gives for the same CSR, from the sampled
+// bands' columns copied to the host (at most the entries of 512 bands of <= 128 rows).
+BandChoice choose_band_device(const int* row_ptr, const int* col, int M, cudaStream_t st);
+
+// The BAND plan's view, bit for bit the one build_band_view makes on the host: a stable segmented
+// sort of each band's entries by column, then one warp per band cuts the greedy 32-column tiles.
+// Checks the view before returning; throws StatusError on failure (nothing is leaked).
+BandLayout build_band_layout(const int* row_ptr, const int* col, const float* val, int M, int64_t nnz, float scale,
+                             int band_rows, cudaStream_t st);
 
 // Checks the invariants the SpMM kernels rely on (index ranges, offsets, item ranges). Blocking.
 bool device_validate(const SegmentLayout* seg, const RowsLayout* rows, int M, int N, int segw, cudaStream_t st);

@@ -553,6 +553,14 @@ VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const i
                               "the device builder needs row_ptr from 0 to nnz and rows with strictly ascending "
                               "columns in [0, N) (vcsrmc_build_host sorts other rows)");
         const float scale = fp32 ? 1.0f : half_scale_from_absmax(dev::device_abs_max(val, nnz, st));
+        // The band height, and for the default plans whether BAND joins them (as for an upload).
+        int band_rows = o.band_rows;
+        if ((band_rows == 0 && (plans & (1 << VCSRMC_PLAN_BAND))) || (o.plans == 0 && !fp32)) {
+            const dev::BandChoice bc = dev::choose_band_device(row_ptr, col, M, st);
+            if (band_rows == 0) band_rows = bc.band_rows;
+            if (o.plans == 0 && !fp32 && bc.entries_per_tile >= dev::kBandMinEntriesPerTile)
+                plans |= 1 << VCSRMC_PLAN_BAND;
+        }
         auto* d = new vcsrmc_device_format;
         d->device = device;
         d->M = M;
@@ -597,34 +605,14 @@ VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const i
             if (!dev::device_validate(d->has_segment ? &seg : nullptr, d->has_rows ? &rows : nullptr, M, N, segw, st))
                 throw StatusError(VCSRMC_INTERNAL, "device-built format failed its index checks");
             if (plans & (1 << VCSRMC_PLAN_BAND)) {
-                // The band view is built on the host from a copy of the CSR (values divided by the
-                // scale, as the row view holds them).
-                dev::RowViewHost rv;
-                rv.rp.resize(size_t(M) + 1);
-                rv.cols.resize(size_t(nnz));
-                rv.vals.resize(size_t(nnz));
-                cuda_check(cudaMemcpyAsync(rv.rp.data(), row_ptr, sizeof(int) * (size_t(M) + 1), cudaMemcpyDeviceToHost, st),
-                           "cudaMemcpyAsync");
-                if (nnz) {
-                    cuda_check(cudaMemcpyAsync(rv.cols.data(), col, sizeof(int) * size_t(nnz), cudaMemcpyDeviceToHost, st),
-                               "cudaMemcpyAsync");
-                    cuda_check(cudaMemcpyAsync(rv.vals.data(), val, sizeof(float) * size_t(nnz), cudaMemcpyDeviceToHost, st),
-                               "cudaMemcpyAsync");
-                }
-                cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
-                const float inv_scale = 1.0f / scale;
-                for (float& x : rv.vals) x *= inv_scale;
-                int H = o.band_rows;
-                if (H == 0) H = dev::choose_band(rv, M).band_rows;
-                dev::BandViewHost bv = dev::build_band_view(rv, M, H, resolve_threads(0));
-                d->band_rows = bv.band_rows;
-                d->n_bands = int(bv.tile_ptr.size()) - 1;
-                d->n_tiles = int64_t(bv.tile_col.size());
-                d->tile_ptr = upload_array(bv.tile_ptr.data(), bv.tile_ptr.size(), st);
-                d->tile_col = upload_array(bv.tile_col.data(), bv.tile_col.size(), st);
-                d->tile_eptr = upload_array(bv.tile_eptr.data(), bv.tile_eptr.size(), st);
-                d->ents = upload_array(bv.ents.data(), bv.ents.size(), st);
-                cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+                dev::BandLayout band = dev::build_band_layout(row_ptr, col, val, M, nnz, scale, band_rows, st);
+                d->band_rows = band.band_rows;
+                d->n_bands = band.n_bands;
+                d->n_tiles = band.n_tiles;
+                d->tile_ptr = band.tile_ptr;
+                d->tile_col = band.tile_col;
+                d->tile_eptr = band.tile_eptr;
+                d->ents = band.ents;
                 d->has_band = true;
             }
             cuda_check(cudaMalloc(&d->status, sizeof(uint32_t)), "cudaMalloc");

@@ -530,25 +530,39 @@ void band_keys(const RowViewHost& rv, int r0, int r1, uint64_t* out) {
 
 }  // namespace
 
-BandChoice choose_band(const RowViewHost& rv, int M) {
+BandChoice choose_band_sampled(int M, const BandSampleFetch& fetch) {
     static const int kCandidates[] = {128, 127, 126, 124, 120, 112, 96, 64};
     BandChoice best{kBandRows, 0.0};
-    double best_cost = 0.0;
-    std::vector<uint64_t> keys;
+    if (M <= 0) return best;
+    // Up to 64 bands spread over the matrix, for every candidate height.
+    std::vector<std::pair<int, int>> ranges;
     for (const int H : kCandidates) {
         const int nb = (M + H - 1) / H;
-        if (nb == 0) return best;
         const int samples = std::min(nb, 64);
-        int64_t tiles = 0, rows = 0, ents = 0;
         for (int k = 0; k < samples; ++k) {
-            const int b = int(int64_t(k) * nb / samples);
-            const int r0 = b * H, r1 = std::min(M, r0 + H);
-            keys.resize(size_t(rv.rp[r1] - rv.rp[r0]));
-            band_keys(rv, r0, r1, keys.data());
-            std::sort(keys.begin(), keys.end());
-            tiles += count_tiles(keys.data(), keys.data() + keys.size());
-            rows += r1 - r0;
-            ents += int64_t(keys.size());
+            const int r0 = int(int64_t(k) * nb / samples) * H;
+            ranges.emplace_back(r0, std::min(M, r0 + H));
+        }
+    }
+    std::vector<const int*> first(ranges.size()), last(ranges.size());
+    fetch(ranges, first, last);
+    double best_cost = 0.0;
+    std::vector<int> cols;
+    size_t i = 0;
+    for (const int H : kCandidates) {
+        const int samples = std::min((M + H - 1) / H, 64);
+        int64_t tiles = 0, rows = 0, ents = 0;
+        for (int k = 0; k < samples; ++k, ++i) {
+            cols.assign(first[i], last[i]);
+            std::sort(cols.begin(), cols.end());
+            int64_t end = -1;  // greedy tiles, as build_band_view cuts them
+            for (const int c : cols)
+                if (c >= end) {
+                    ++tiles;
+                    end = int64_t(c) + kBandK;
+                }
+            rows += ranges[i].second - ranges[i].first;
+            ents += int64_t(cols.size());
         }
         // tensor-core tiles per row, plus the epilogue of a band (about two tiles' time)
         const double cost = (double(tiles) + 2.0 * samples) / double(std::max<int64_t>(rows, 1));
@@ -558,6 +572,16 @@ BandChoice choose_band(const RowViewHost& rv, int M) {
         }
     }
     return best;
+}
+
+BandChoice choose_band(const RowViewHost& rv, int M) {
+    return choose_band_sampled(M, [&](const std::vector<std::pair<int, int>>& ranges, std::vector<const int*>& first,
+                                      std::vector<const int*>& last) {
+        for (size_t i = 0; i < ranges.size(); ++i) {
+            first[i] = rv.cols.data() + rv.rp[size_t(ranges[i].first)];
+            last[i] = rv.cols.data() + rv.rp[size_t(ranges[i].second)];
+        }
+    });
 }
 
 BandViewHost build_band_view(const RowViewHost& rv, int M, int band_rows, int nthreads) {

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <functional>
+#include <utility>
 #include <vector>
 
 #include "plan_rows.hpp"
@@ -35,6 +37,13 @@ struct BandChoice {
     double entries_per_tile;
 };
 BandChoice choose_band(const RowViewHost& rv, int M);
+
+// The same choice from any source of the sampled bands: fetch(ranges, first, last) makes
+// [first[i], last[i]) the columns (any order) of the entries of rows [ranges[i].first,
+// ranges[i].second), in host memory that stays valid until the chooser returns.
+using BandSampleFetch = std::function<void(const std::vector<std::pair<int, int>>& ranges,
+                                           std::vector<const int*>& first, std::vector<const int*>& last)>;
+BandChoice choose_band_sampled(int M, const BandSampleFetch& fetch);
 
 // From the row view (rows' entries in ascending column order, values already divided by the
 // format's scale). nthreads <= 0: all host threads.
