@@ -299,7 +299,7 @@ def main() -> None:
     ap.add_argument("--segw", type=int, default=32)
     ap.add_argument("--tileK", type=int, default=128)
     ap.add_argument("--plan", choices=["rows", "segment", "band"], default="rows")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=12)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
@@ -548,10 +548,42 @@ def main() -> None:
         e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], dtype=torch.float64, device="cuda")
         if dist is not None:
             dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        # The link's own floor for one step: this rank's B upload and C download timed alone and
+        # together (the two directions of PCIe run at once), the same bytes as a step.
+        def copy_ms(up: bool, down: bool) -> float:
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            up_stream.wait_stream(stream)
+            down_stream.wait_stream(stream)
+            if up:
+                with torch.cuda.stream(up_stream):
+                    (Bpiece[0] if world > 1 else Bd[0]).copy_(hB, non_blocking=True)
+            if down:
+                with torch.cuda.stream(down_stream):
+                    hC.copy_(Cd[0], non_blocking=True)
+            stream.wait_stream(up_stream)
+            stream.wait_stream(down_stream)
+            b.record(stream)
+            torch.cuda.synchronize()
+            return a.elapsed_time(b)
+
+        up_ms, down_ms, both_ms = copy_ms(True, False), copy_ms(False, True), copy_ms(True, True)
+        link = torch.tensor([up_ms, down_ms, both_ms], dtype=torch.float64, device="cuda")
+        if dist is not None:
+            dist.all_reduce(link, op=dist.ReduceOp.MAX)
+        up_ms, down_ms, both_ms = (float(x) for x in link.tolist())
         e2e = {"value": flops / (float(e2e_ms) * 1e-3) / 1e9, "unit": "GFLOP/s",
                "h2d_bytes_per_step": int(hB.numel() * hB.element_size()),
                "d2h_bytes_per_step": int(hC.numel() * hC.element_size()), "ms_per_step": float(e2e_ms),
                "pipelining": "upload of step i+1 overlaps download of step i (two device buffers, two copy streams)",
+               "steps": args.e2e_steps,
+               "link": {"h2d_ms": up_ms, "d2h_ms": down_ms, "both_ms": both_ms,
+                        "h2d_GBps": hB.numel() * hB.element_size() / (up_ms * 1e-3) / 1e9,
+                        "d2h_GBps": hC.numel() * hC.element_size() / (down_ms * 1e-3) / 1e9,
+                        "floor_ms_per_step": both_ms,
+                        "frac": both_ms / float(e2e_ms),
+                        "how": "this step's H2D and D2H copies timed alone and at once, max over ranks"},
                "b_staging": ("each rank uploads 1/N of B, NCCL all-gather over NVLink" if world > 1 else
                              "B uploaded whole")}
         del Bd, Cd, hB, hC
