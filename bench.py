@@ -329,7 +329,7 @@ def main() -> None:
                        ("CUDA-core FFMA" if (args.plan == "rows" or not fp16) else "tcgen05 MMA, TMEM accumulator")),
               "plan": {"rows": "rows: row-stationary over the VCSR-MC row view, C stored once",
                        "segment": "segment: reference dataflow, per-item B segment, C reductions",
-                       "band": "band: 128-row bands x 32-column tiles on tcgen05, TMEM accumulator, C stored once"}[args.plan],
+                       "band": "band: 128-row bands x {band_cols}-column tiles on tcgen05, TMEM accumulator, C stored once"}[args.plan],
               "parallelism": f"row-shard x{args.gpus} (balanced on nnz + {args.row_weight} x rows), B replicated",
               "l2": None}
 
@@ -341,6 +341,7 @@ def main() -> None:
         # The reference's own CPU implementation of the path (oracle/_ref), rank 0 only.
         if rank != 0:
             return
+        config["plan"] = config["plan"].format(band_cols="kBandK")
         try:
             M, N, rp, col, val = load_or_generate_csr(spec, 0, 1, lambda: None)
             cb = time_reference_cpu(M, N, rp, col, val, args.steps, args.warmup, args.cpu_sample_nnz, fp16)
@@ -404,6 +405,7 @@ def main() -> None:
     # split into chunks that are reduced into C
     launches_per_step = 1 + (1 if plan == vm.PLAN_ROWS and info["n_split_rows"] > 0 else 0)
     groups, slots, items = info["n_groups"], info["n_slots"], info["n_items"]
+    config["plan"] = config["plan"].format(band_cols=info["band_cols"])
     log(f"rank {rank}: rows [{r0},{r1}) nnz {p1 - p0} format build + upload ({args.build}) {build_s:.2f}s "
         f"setup {time.time() - t0:.1f}s")
 
@@ -656,7 +658,7 @@ def main() -> None:
                        "groups": groups, "slots": slots, "items": items, "device_status": status,
                        "format_build": args.build, "format_build_upload_s": build_s,
                        "rows_unit_nnz": info["rows_unit_nnz"], "band_rows": info["band_rows"],
-                       "clock_samples": clk["samples"]},
+                       "band_tiles": info["n_tiles"], "clock_samples": clk["samples"]},
         }
         emit(line)
     dV.free()

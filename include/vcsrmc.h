@@ -47,7 +47,7 @@ extern "C" {
  *          segment once, multiply every 16-row group, add it into C with reductions.
  * ROWS:    row-stationary over the format's row view (built at upload): each C row is
  *          accumulated in registers from gathered B rows and stored once.
- * BAND:    FP16 format only: bands of 128 rows, tiles of 32 columns multiplied on the tensor
+ * BAND:    FP16 format only: bands of <= 128 rows, tiles of 64 columns multiplied on the tensor
  *          cores into one accumulator per band, C stored once. For matrices whose rows touch
  *          few column windows (stencils, banded or reordered matrices).
  * AUTO:    the first resident layout of BAND (fp16 B only), ROWS, SEGMENT, BAND.          */
@@ -141,7 +141,7 @@ void vcsrmc_format_free(vcsrmc_format* f);
 int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out);
 /* Same, choosing which plan layouts to make resident: a bit mask of (1 << VCSRMC_PLAN_SEGMENT),
  * (1 << VCSRMC_PLAN_ROWS) and (1 << VCSRMC_PLAN_BAND). 0 (what vcsrmc_upload does) = SEGMENT and
- * ROWS, plus BAND for an FP16 format whose 128-row x 32-column tiles hold enough entries to
+ * ROWS, plus BAND for an FP16 format whose band x 64-column tiles hold enough entries to
  * beat ROWS (estimated from a sample of bands). */
 int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans, void* stream,
                      vcsrmc_device_format** out);
@@ -185,6 +185,7 @@ typedef struct {
     int32_t rows_unit_nnz, n_split_rows;  /* ROWS: entries per unit, rows split into chunks */
     int32_t band_rows, n_bands;           /* BAND layout                                    */
     int64_t n_tiles;
+    int32_t band_cols, reserved;          /* BAND: columns per tile (this build's tile width) */
 } vcsrmc_device_info;
 int vcsrmc_device_info_get(const vcsrmc_device_format* d, vcsrmc_device_info* out);
 /* Error flags raised by kernels of this format since the last clear (bit 0: a bounded wait

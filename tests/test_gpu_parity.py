@@ -231,9 +231,9 @@ def test_dense_device_generator_matches_host(cuda):
     assert np.array_equal(d16.cpu().numpy(), h.astype(np.float16))
 
 
-@pytest.mark.parametrize("n", [1, 100, 128, 129, 300])
+@pytest.mark.parametrize("n", [1, 40, 100, 128, 129, 300])
 def test_band_plan_shapes(cuda, n):
-    """BAND plan: partial last band, bands without entries, tiles at the last columns, N < 32."""
+    """BAND plan: partial last band, bands without entries, tiles at the last columns, N below the tile width."""
     rp, col, val = random_csr(n, n, min(1.0, 6.0 / n), seed=n, empty_rows=True)
     A = vm.CSR.from_arrays(n, n, rp, col, val)
     B = np.random.default_rng(n).uniform(-1, 1, size=(n, 128)).astype(np.float32)

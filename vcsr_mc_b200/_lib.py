@@ -38,7 +38,7 @@ class DeviceInfo(ctypes.Structure):
                 ("n_groups", ctypes.c_int64), ("n_slots", ctypes.c_int64), ("n_items", ctypes.c_int64),
                 ("n_units", ctypes.c_int64), ("rows_unit_nnz", ctypes.c_int32), ("n_split_rows", ctypes.c_int32),
                 ("band_rows", ctypes.c_int32), ("n_bands", ctypes.c_int32),
-                ("n_tiles", ctypes.c_int64)]
+                ("n_tiles", ctypes.c_int64), ("band_cols", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class UploadOptions(ctypes.Structure):

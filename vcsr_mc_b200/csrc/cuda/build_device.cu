@@ -305,20 +305,20 @@ __global__ void band_offsets_kernel(const int* __restrict__ rp, int M, int H, in
         boff[b] = rp[int64_t(b) * H < M ? int64_t(b) * H : int64_t(M)];
 }
 
-// An entry's view word without its local column: row within the band (bits 5-11) and the fp16 bits
-// of value / scale (bits 16-31). One warp per row.
+// An entry's view word without its local column: row within the band (the 7 bits above the local
+// column's) and the fp16 bits of value / scale (bits 16-31). One warp per row.
 __global__ void band_payload_kernel(const int* __restrict__ rp, const float* __restrict__ val, int M, int H,
                                     float inv_scale, uint32_t* __restrict__ payload) {
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = int64_t(gridDim.x) * (blockDim.x >> 5);
     for (int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < M; r += nwarps) {
-        const uint32_t row = uint32_t(r % H) << 5;
+        const uint32_t row = uint32_t(r % H) << kBandColBits;
         for (int p = rp[r] + lane; p < rp[r + 1]; p += 32)
             payload[p] = row | (uint32_t(__half_as_ushort(__float2half_rn(val[p] * inv_scale))) << 16);
     }
 }
 
-// Greedy 32-column tiles over a band's entries sorted by column: a tile starts at the first
+// Greedy kBandK-column tiles over a band's entries sorted by column: a tile starts at the first
 // column at or past the end of the previous tile. One warp per band walks its entries 32 at a
 // time; inside a chunk, the next start is the first lane (ballot) whose column reaches the current
 // end, repeated while one does. kWrite = false counts the tiles; kWrite = true writes tile_col,
@@ -350,7 +350,7 @@ __global__ void band_tiles_kernel(const int* __restrict__ boff, const int* __res
                 ++t;
                 if (lane >= L) mine = s;
                 start = s;
-                end = int64_t(s) + 32;
+                end = int64_t(s) + kBandK;
                 pend = __ballot_sync(0xffffffffu, valid && c >= end);
             }
             if (kWrite && valid) ents[i] |= uint32_t(c - mine);
@@ -360,7 +360,7 @@ __global__ void band_tiles_kernel(const int* __restrict__ boff, const int* __res
 }
 
 // The checks build_band_view makes on the host: per band, tiles in range, covering exactly the
-// band's entries, each non-empty, starts ascending by at least 32 columns.
+// band's entries, each non-empty, starts ascending by at least kBandK columns.
 __global__ void validate_band_kernel(const int* __restrict__ boff, const int* __restrict__ tile_ptr,
                                      const int* __restrict__ tile_col, const int* __restrict__ tile_eptr, int nb,
                                      int64_t T, int* bad) {
@@ -374,7 +374,7 @@ __global__ void validate_band_kernel(const int* __restrict__ boff, const int* __
         if ((t1 > t0 && (tile_eptr[t0] != e0 || tile_eptr[t1] != e1)) || (t1 == t0 && e1 != e0)) atomicOr(bad, 2);
         for (int t = t0; t < t1; ++t) {
             if (tile_eptr[t + 1] <= tile_eptr[t] || tile_col[t] < 0 ||
-                (t > t0 && int64_t(tile_col[t]) < int64_t(tile_col[t - 1]) + 32))
+                (t > t0 && int64_t(tile_col[t]) < int64_t(tile_col[t - 1]) + kBandK))
                 atomicOr(bad, 4);
         }
     }

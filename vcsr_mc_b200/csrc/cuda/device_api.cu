@@ -452,6 +452,7 @@ VCSRMC_EXPORT int vcsrmc_device_info_get(const vcsrmc_device_format* d, vcsrmc_d
         i.band_rows = d->band_rows;
         i.n_bands = d->n_bands;
         i.n_tiles = d->n_tiles;
+        i.band_cols = dev::kBandK;
         *out = i;
     });
 }

@@ -6,21 +6,24 @@
 // one segment by that segment's rows of B and adds every group into C with atomics. Here the
 // same tcgen05 tile product (A densified from (column, value) entries in shared memory, B staged
 // by TMA with the 128-byte swizzle, fp32 accumulation) runs row-stationary:
-//   * a tile = a band's entries in 32 consecutive columns starting at the first column not
-//     covered by the previous tile; each adds a (band x 32) by (32 x 128) product into the
-//     band's TMEM accumulator (M = 128, N = 128, two K = 16 steps);
+//   * a tile = a band's entries in kBandK (64) consecutive columns starting at the first column
+//     not covered by the previous tile; each adds a (band x 64) by (64 x 128) product into the
+//     band's TMEM accumulator (M = 128, N = 128, four K = 16 steps);
 //   * persistent CTAs (two per SM) walk their work items (band, slab) in a strided order; the
-//     tiles of all their items form one sequence through 5 shared-memory stages (B 8 KB, A
-//     8 KB). Producer warp w owns stage w: once the MMAs of its previous tile have completed it
+//     tiles of all their items form one sequence through 3 shared-memory stages (B 16 KB, A
+//     16 KB). Producer warp w owns stage w: once the MMAs of its previous tile have completed it
 //     starts the TMA load of its next B tile, prefetches the one after into L2, clears its
 //     previous entries from the A tile (the positions it remembers, or the whole tile after a
 //     large one), writes the new entries and arrives on the stage's barrier. Its registers run
 //     one position ahead (entries and bounds are loaded two iterations before use);
 //   * lane 0 of the MMA warp issues the MMAs in sequence order into one of two TMEM
 //     accumulators (256 columns), so the MMAs of a band overlap the epilogue of the previous one;
-//   * four epilogue warps read their TMEM lane quarter (tcgen05.ld), transpose 32 x 32 blocks
-//     through shared memory and write C with whole 128-byte lines (read once for C += A*B).
-// B traffic per band is the B rows of its tiles (32 x 256 bytes each), which neighbouring bands
+//   * four epilogue warps read their TMEM lane quarter (tcgen05.ld), transpose 32 x 16 blocks
+//     through shared memory and write C in whole 32-byte sectors (read once for C += A*B).
+// Two CTAs per SM outrun one CTA with twice the stages (0.300 against 0.365 ms on a 27-point
+// stencil): each CTA's MMA issuer walks its tiles one at a time, and the second CTA fills its
+// waits. 64-column tiles beat 32-column ones (0.317 ms) by halving the tiles.
+// B traffic per band is the B rows of its tiles (64 x 256 bytes each), which neighbouring bands
 // share in L2; this suits matrices whose rows touch few column windows (stencils, banded or
 // reordered matrices). Matrices with scattered columns are served better by the ROWS plan.
 // Every wait is bounded; on expiry the CTA's warps stop, drain what they issued, the format's
@@ -43,23 +46,34 @@ namespace vcsrmc {
 namespace dev {
 namespace {
 
+// Build-time shape: stages per CTA and CTAs per SM share the SM's shared memory (a stage holds a
+// kBandK-row B tile and a 128 x kBandK A tile).
+#ifndef VCSRMC_BAND_STAGES
+#define VCSRMC_BAND_STAGES (kBandK == 64 ? 3 : 5)
+#endif
+#ifndef VCSRMC_BAND_CTAS
+#define VCSRMC_BAND_CTAS 2
+#endif
 constexpr int kSlab = 128;                       // columns of B and C per work item = MMA N
-constexpr int kStages = 5;
-constexpr int kProducers = kStages;              // warps 0-4: producer w fills stage w
-constexpr int kMmaWarp = kProducers;             // warp 5: lane 0 issues the MMAs
-constexpr int kEpiWarp0 = kProducers + 1;        // warps 6-9: epilogue (TMEM lane quarter = warp % 4)
+constexpr int kStages = VCSRMC_BAND_STAGES;
+constexpr int kProducers = kStages;              // warps 0 .. kStages - 1: producer w fills stage w
+constexpr int kMmaWarp = kProducers;             // next warp: lane 0 issues the MMAs
+constexpr int kEpiWarp0 = kProducers + 1;        // last 4 warps: epilogue (TMEM lane quarter = warp % 4)
 constexpr int kWarps = kEpiWarp0 + 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kCtasPerSm = 2;
+constexpr int kCtasPerSm = VCSRMC_BAND_CTAS;
 constexpr int kSaved = 8;                        // entries a producer lane keeps per tile (to clear them)
 constexpr int kAccs = 2;                         // TMEM accumulators: one band's MMAs overlap the previous epilogue
 constexpr uint32_t kTmemCols = kAccs * kSlab;
-constexpr int kPanelBytes = kBandK * 128;        // 32 rows x 64 fp16, 128-byte swizzle
+constexpr int kPanelBytes = kBandK * 128;        // kBandK rows x 64 fp16, 128-byte swizzle
 constexpr int kBBytes = 2 * kPanelBytes;
 constexpr int kABytes = kBandRows * kBandK * 2;
 constexpr int kStageBytes = kBBytes + kABytes;   // a multiple of 1024: swizzle atoms stay aligned
-constexpr int kEpiStride = 36;                   // floats per row of an epilogue warp's 32 x 32 staging tile
-constexpr int kEpiBytes = 32 * kEpiStride * 4;
+// Epilogue staging: 32 rows x 16 columns of fp32 per warp, the 16-byte chunk j of row r at
+// chunk position j ^ ((r >> 1) & 3), so that both the row-per-lane writes and the
+// row-segment reads of a quarter warp touch 8 distinct 4-bank groups.
+constexpr int kEpiCols = 16;
+constexpr int kEpiBytes = 32 * kEpiCols * 4;
 constexpr int kEpiOffset = kStages * kStageBytes;
 constexpr int kBarOffset = kEpiOffset + 4 * kEpiBytes;
 constexpr int kNumBars = 3 * kStages + 2 * kAccs;
@@ -67,13 +81,16 @@ constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // + barriers
 static_assert(kStageBytes % 1024 == 0, "stage alignment");
 static_assert(kCtasPerSm * kTmemCols <= 512, "tensor memory per SM");
 static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 233472, "shared memory per SM");
+static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 
 // Byte offset of A element (row r, column c) in the K-major, unswizzled A tile: core matrices of
 // 8 rows x 16 bytes, K-adjacent ones 128 B apart (LBO), 8-row blocks kBandK * 16 B apart (SBO).
 __device__ __forceinline__ int a_offset(int r, int c) {
     return ((r >> 3) * (kBandK / 8) + (c >> 3)) * 128 + (r & 7) * 16 + (c & 7) * 2;
 }
-__device__ __forceinline__ int ent_offset(uint32_t e) { return a_offset(int((e >> 5) & 127u), int(e & 31u)); }
+__device__ __forceinline__ int ent_offset(uint32_t e) {
+    return a_offset(int((e >> kBandColBits) & 127u), int(e & uint32_t(kBandK - 1)));
+}
 
 __device__ __forceinline__ __half to_half(float v) { return __float2half_rn(v); }
 __device__ __forceinline__ __half to_half(__half v) { return v; }
@@ -395,31 +412,33 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 const uint32_t acc = u % kAccs;
                 if (!__all_sync(0xffffffffu, wait_or_abort(&acc_full[acc], (u / kAccs) & 1u, abort_flag))) break;
                 tc_fence_after();
-                // 32 rows x 32 columns at a time: TMEM -> registers (thread = row) -> shared
-                // memory -> registers (8 lanes = one 128-byte row segment) -> C, so that every
-                // warp store writes four whole 128-byte lines
+                // 32 rows x 16 columns at a time: TMEM -> registers (thread = row) -> shared
+                // memory -> registers (4 lanes = one 64-byte row segment) -> C, so that a warp
+                // store writes 8 rows' segments of two whole 32-byte sectors each
                 float* stage_c = reinterpret_cast<float*>(smem + kEpiOffset + quarter * kEpiBytes);
                 const int nrows = min(32, row_end - (row0 + quarter * 32));  // may be <= 0
+                const int sw_w = (lane >> 1) & 3;  // this lane's row swizzle (row = lane)
 #pragma unroll 1
-                for (int c = 0; c < kSlab; c += 32) {
+                for (int c = 0; c < kSlab; c += kEpiCols) {
                     if (c >= ncols) break;
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(tmem + lane_base + acc * kSlab + uint32_t(c), v);
+                    uint32_t v[kEpiCols];
+                    tmem_ld_32x32b_x16(tmem + lane_base + acc * kSlab + uint32_t(c), v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        *reinterpret_cast<float4*>(stage_c + lane * kEpiStride + 4 * j) =
+                    for (int j = 0; j < kEpiCols / 4; ++j)
+                        *reinterpret_cast<float4*>(stage_c + lane * kEpiCols + 4 * (j ^ sw_w)) =
                             make_float4(__uint_as_float(v[4 * j]) * P.scale, __uint_as_float(v[4 * j + 1]) * P.scale,
                                         __uint_as_float(v[4 * j + 2]) * P.scale,
                                         __uint_as_float(v[4 * j + 3]) * P.scale);
                     __syncwarp();
-                    const int cq = 4 * (lane & 7);  // this lane's 4 columns of a row segment
-                    const int col = c + cq;
+                    const int cj = lane & 3;  // this lane's 4-column chunk of a row segment
+                    const int col = c + 4 * cj;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int rr = 4 * i + (lane >> 3);
+                    for (int i = 0; i < 4; ++i) {
+                        const int rr = 8 * i + (lane >> 2);
                         if (rr < nrows) {
-                            float4 x = *reinterpret_cast<const float4*>(stage_c + rr * kEpiStride + cq);
+                            float4 x = *reinterpret_cast<const float4*>(stage_c + rr * kEpiCols +
+                                                                        4 * (cj ^ ((rr >> 1) & 3)));
                             float* dst = C + int64_t(row0 + quarter * 32 + rr) * ldc + k0 + col;
                             if (vec_c && col + 3 < ncols) {
                                 if constexpr (kAcc) {
@@ -438,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                             }
                         }
                     }
-                    __syncwarp();  // the staging tile is rewritten by the next 32 columns
+                    __syncwarp();  // the staging tile is rewritten by the next 16 columns
                 }
                 tc_fence_before();
                 mbar_arrive(&acc_empty[acc]);
@@ -509,7 +528,7 @@ uint64_t band_key(int col, int row_in_band, float v) {
 }
 
 // Greedy tiles over a band's keys sorted by column: a tile starts at the first column not yet
-// covered and covers 32 columns. Returns the number of tiles.
+// covered and covers kBandK columns. Returns the number of tiles.
 int64_t count_tiles(const uint64_t* kb, const uint64_t* ke) {
     int64_t n = 0;
     int64_t end = -1;  // first column past the current tile
@@ -627,7 +646,7 @@ BandViewHost build_band_view(const RowViewHost& rv, int M, int band_rows, int nt
                     h.tile_eptr[size_t(t)] = p;
                 }
                 const uint32_t row = uint32_t(k >> 16) & 0x7fu, bits = uint32_t(k & 0xffffu);
-                h.ents[size_t(p)] = uint32_t(c - start) | (row << 5) | (bits << 16);
+                h.ents[size_t(p)] = uint32_t(c - start) | (row << kBandColBits) | (bits << 16);
             }
         }
     });

@@ -12,18 +12,25 @@
 namespace vcsrmc {
 namespace dev {
 
-constexpr int kBandRows = 128;  // rows per band at most = tcgen05 tile M
-constexpr int kBandK = 32;      // columns of A (= rows of B) per tile: two K = 16 MMA steps
-// Below this many entries per tile the ROWS plan is faster (measured on a B200: about 1.1 ns of
-// tensor-core pipeline per tile against 0.025-0.045 ns per gathered entry for ROWS).
-constexpr double kBandMinEntriesPerTile = 40.0;
+#ifndef VCSRMC_BAND_K
+#define VCSRMC_BAND_K 64
+#endif
+constexpr int kBandRows = 128;          // rows per band at most = tcgen05 tile M
+constexpr int kBandK = VCSRMC_BAND_K;   // columns of A (= rows of B) per tile: kBandK / 16 MMA K steps
+constexpr int kBandColBits = kBandK == 64 ? 6 : 5;  // bits of an entry's column within its tile
+static_assert(kBandK == 32 || kBandK == 64, "tiles of 32 or 64 columns");
+// Below this many entries per tile the ROWS plan is faster (measured on a B200: about 2.3 ns of
+// tensor-core pipeline per 64-column tile, 1.3 ns per 32-column one, against 0.025-0.045 ns per
+// gathered entry for ROWS).
+constexpr double kBandMinEntriesPerTile = kBandK == 64 ? 64.0 : 40.0;
 
 // Host-side band view. Band b covers rows [b * band_rows, (b + 1) * band_rows). Its tiles are
 // [tile_ptr[b], tile_ptr[b+1]) in ascending column order; tile t covers columns
-// [tile_col[t], tile_col[t] + 32) and holds entries [tile_eptr[t], tile_eptr[t+1]). A tile starts
-// at the first column of the band not covered by the previous tile, so a window of w
-// consecutive occupied columns takes ceil(w / 32) tiles wherever it starts. An entry packs the
-// local column (bits 0-4), the row within the band (bits 5-11) and the fp16 value (bits 16-31).
+// [tile_col[t], tile_col[t] + kBandK) and holds entries [tile_eptr[t], tile_eptr[t+1]). A tile
+// starts at the first column of the band not covered by the previous tile, so a window of w
+// consecutive occupied columns takes ceil(w / kBandK) tiles wherever it starts. An entry packs
+// the local column (bits 0 .. kBandColBits - 1), the row within the band (the next 7 bits) and
+// the fp16 value (bits 16-31).
 struct BandViewHost {
     int band_rows = kBandRows;
     std::vector<int> tile_ptr, tile_col, tile_eptr;
