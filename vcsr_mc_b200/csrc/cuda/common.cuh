@@ -76,6 +76,18 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
         ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
+// Four rows of a 2-D tensor (a box one row high, x .. x + box width) into consecutive rows of
+// this CTA's shared memory, completion on `bar`. The tensor map's box must be one row high and x
+// a multiple of 16 bytes.
+__device__ __forceinline__ void tma_gather4_2d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y0, int y1,
+                                               int y2, int y3) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
+        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y0),
+          "r"(y1), "r"(y2), "r"(y3)
+        : "memory");
+}
 // Brings a 2-D box of the tensor into L2 (no shared memory, no completion to wait for).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int x, int y) {
     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"

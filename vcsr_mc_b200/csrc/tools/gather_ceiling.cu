@@ -1,16 +1,28 @@
 // gather_ceiling: the achievable rate of random 256-byte row gathers on this GPU (the memory
 // pattern of the ROWS SpMM plan, without its sparse bookkeeping). B = 2^24 rows x 128 fp16
 // (4.3 GB); 2^26 row indices drawn uniformly from the first `span` rows (mode 0: all rows,
-// 1: 2^20 rows = 268 MB, 2: 2^17 rows = 34 MB, i.e. L2-resident). A 16-lane group loads 16
-// indices coalesced and gathers them in rounds of 8 rows whose loads are issued together; each
-// lane sums its 16 bytes of each row. Reports rows/s and gathered TB/s per launch shape.
+// 1: 2^20 rows = 268 MB, 2: 2^17 rows = 34 MB, i.e. L2-resident). Two ways to gather:
+//   * registers: a 16-lane group loads 16 indices coalesced and gathers them in rounds of 8 rows
+//     whose loads are issued together; each lane sums its 16 bytes of each row;
+//   * TMA tile::gather4: each warp keeps a ring of kDepth 1-KB slots in shared memory, lane 0
+//     fills a slot with four B rows per instruction (completion on the slot's mbarrier) and the
+//     warp sums the slot, so the rows in flight per SM are set by shared memory, not registers.
+// B holds ((r % 61) + (c % 3)) / 64, so the exact sum of every gathered row is known on the host
+// and the TMA path's result is checked against it. Reports rows/s and gathered TB/s per shape.
 //   vcsr_mc_b200/gather_ceiling [mode]
 #include <cuda_fp16.h>
+#include <cuda.h>
 #include <cstdio>
 #include <cstdint>
 #include <cstdlib>
+#include <cstring>
 #include <vector>
 #include <random>
+
+#include "../cuda/common.cuh"
+#include "../cuda/tma_host.hpp"
+
+using namespace vcsrmc::dev;
 
 __device__ __forceinline__ void ld8(const uint4* p0, const uint4* p1, const uint4* p2, const uint4* p3,
                                     const uint4* p4, const uint4* p5, const uint4* p6, const uint4* p7, uint4 (&r)[8]) {
@@ -95,18 +107,133 @@ void run(const uint4* B, const unsigned* idx, long long n, float* out, const cha
            n / (ms * 1e6), n * 256.0 / (ms * 1e9));
 }
 
+__global__ void fill_b(__half* B, long long nrows) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nrows * 128; i += (long long)gridDim.x * blockDim.x)
+        B[i] = __float2half(float((i / 128) % 61 + (i % 128) % 3) / 64.f);
+}
+
+// kWarps warps per CTA, each with its own ring of kDepth slots; warp w of CTA b gathers indices
+// [p0, p0 + per_warp), p0 = (b * kWarps + w) * per_warp, four per slot. Every wait is bounded: on
+// expiry the warp drains what it issued (bounded), sets *err and stops.
+template <int kWarps, int kDepth>
+__global__ void __launch_bounds__(kWarps * 32) gather4_tma(const __grid_constant__ CUtensorMap tmap,
+                                                           const uint4* __restrict__ idx4, long long n, int per_warp,
+                                                           double* __restrict__ out, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* ring = smem + warp * kDepth * 1024;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kDepth * 1024) + warp * kDepth;
+    const long long gw = (long long)blockIdx.x * kWarps + warp;
+    const long long p0 = gw * per_warp;
+    if (p0 >= n) return;
+    const long long p1 = p0 + per_warp < n ? p0 + per_warp : n;
+    const int nq = int((p1 - p0) / 4);
+    const long long g0 = p0 / 4;
+    if (lane == 0) {
+        for (int s = 0; s < kDepth; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+        prefetch_tmap(&tmap);
+    }
+    __syncwarp();
+    uint4 ynext = make_uint4(0, 0, 0, 0);
+    auto issue = [&](int q, uint4 y) {
+        const int s = q % kDepth;
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&bars[s], 1024u);
+        tma_gather4_2d(ring + s * 1024, &tmap, &bars[s], 0, int(y.x), int(y.y), int(y.z), int(y.w));
+    };
+    const int pre = nq < kDepth ? nq : kDepth;
+    if (lane == 0) {
+        for (int q = 0; q < pre; ++q) issue(q, __ldg(idx4 + g0 + q));
+        if (pre < nq) ynext = __ldg(idx4 + g0 + pre);
+    }
+    int issued = pre;
+    float acc = 0.f;
+    int q = 0;
+    for (; q < nq; ++q) {
+        const int s = q % kDepth;
+        const bool ok = mbar_wait_bounded(&bars[s], uint32_t(q / kDepth) & 1u);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        const uint4* src = reinterpret_cast<const uint4*>(ring + s * 1024) + lane * 2;
+        const uint4 a = src[0], b = src[1];
+        const __half2* h0 = reinterpret_cast<const __half2*>(&a);
+        const __half2* h1 = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f0 = __half22float2(h0[i]), f1 = __half22float2(h1[i]);
+            acc += (f0.x + f0.y) + (f1.x + f1.y);
+        }
+        __syncwarp();  // every lane has read slot s before it is refilled
+        if (lane == 0 && issued < nq) {
+            issue(issued, ynext);
+            ++issued;
+            if (issued < nq) ynext = __ldg(idx4 + g0 + issued);
+        }
+        issued = __shfl_sync(0xffffffffu, issued, 0);
+    }
+    if (q < nq) {  // a wait expired: let the loads already issued land, then report
+        if (lane == 0) {
+            for (int r = q; r < issued; ++r) mbar_wait_bounded(&bars[r % kDepth], uint32_t(r / kDepth) & 1u);
+            atomicOr(err, 1);
+        }
+        return;
+    }
+    double d = acc;
+    for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    if (lane == 0) out[gw] = d;
+}
+
+template <int kWarps, int kDepth>
+void run_tma(const CUtensorMap& tmap, const unsigned* idx, long long n, double* out, int* err, double expect) {
+    const int per_warp = 4096;
+    const long long warps = (n + per_warp - 1) / per_warp;
+    const long long blocks = (warps + kWarps - 1) / kWarps;
+    const int smem = kWarps * kDepth * 1024 + kWarps * kDepth * 8 + 1024;
+    auto k = gather4_tma<kWarps, kDepth>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        printf("tma      W=%2d D=%2d: shared memory %d B not available\n", kWarps, kDepth, smem);
+        return;
+    }
+    cudaMemset(out, 0, warps * sizeof(double));
+    cudaEvent_t a, b; cudaEventCreate(&a); cudaEventCreate(&b);
+    for (int w = 0; w < 2; ++w) k<<<blocks, kWarps * 32, smem>>>(tmap, reinterpret_cast<const uint4*>(idx), n, per_warp, out, err);
+    cudaEventRecord(a);
+    const int reps = 5;
+    for (int w = 0; w < reps; ++w) k<<<blocks, kWarps * 32, smem>>>(tmap, reinterpret_cast<const uint4*>(idx), n, per_warp, out, err);
+    cudaEventRecord(b); cudaEventSynchronize(b);
+    float ms; cudaEventElapsedTime(&ms, a, b);
+    ms /= reps;
+    std::vector<double> h(warps);
+    cudaMemcpy(h.data(), out, warps * sizeof(double), cudaMemcpyDeviceToHost);
+    int herr = 0;
+    cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost);
+    double sum = 0;
+    for (double x : h) sum += x;
+    int nb = 0; cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, kWarps * 32, smem);
+    printf("tma      W=%2d D=%2d warps/SM=%2d rows in flight/SM=%4d : %.3f ms  %6.2f G rows/s  %.2f TB/s  sum %s%s\n",
+           kWarps, kDepth, nb * kWarps, nb * kWarps * kDepth * 4, ms, n / (ms * 1e6), n * 256.0 / (ms * 1e9),
+           sum == expect ? "exact" : "WRONG", herr ? " (a wait expired)" : "");
+}
+
 int main(int argc, char** argv) {
     const long long nrows = 1LL << 24;  // 16.8M rows x 256 B = 4.3 GB
     const long long n = 1LL << 26;      // gathers
     const int mode = argc > 1 ? atoi(argv[1]) : 0;
-    uint4* B; unsigned* idx; float* out;
+    uint4* B; unsigned* idx; float* out; double* dout; int* err;
     if (cudaMalloc(&B, nrows * 256) != cudaSuccess) { printf("oom\n"); return 1; }
-    cudaMemset(B, 0, nrows * 256);
-    cudaMalloc(&idx, n * 4); cudaMalloc(&out, 1 << 24);
+    fill_b<<<148 * 16, 256>>>(reinterpret_cast<__half*>(B), nrows);
+    cudaMalloc(&idx, n * 4); cudaMalloc(&out, 1 << 24); cudaMalloc(&dout, (n / 4096 + 1) * sizeof(double));
+    cudaMalloc(&err, sizeof(int)); cudaMemset(err, 0, sizeof(int));
     std::vector<unsigned> h(n);
     std::mt19937_64 rng(1);
     const long long span = mode == 0 ? nrows : (mode == 1 ? (1LL << 20) : (1LL << 17));
-    for (auto& x : h) x = unsigned(rng() % span);
+    double expect = 0;
+    for (auto& x : h) {
+        x = unsigned(rng() % span);
+        expect += 2.0 * (x % 61) + 127.0 / 64.0;  // sum of row x of B
+    }
     cudaMemcpy(idx, h.data(), n * 4, cudaMemcpyHostToDevice);
     printf("mode %d: rows uniform over %lld (%.0f MB)\n", mode, span, span * 256.0 / 1e6);
     run<8, false>(B, idx, n, out, "single");
@@ -114,6 +241,24 @@ int main(int argc, char** argv) {
     run<4, true>(B, idx, n, out, "double");
     run<16, true>(B, idx, n, out, "double");
     run<16, false>(B, idx, n, out, "single");
+    CUtensorMap tmap;
+    std::memset(&tmap, 0, sizeof tmap);
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    const cuuint64_t dims[2] = {128u, cuuint64_t(nrows)};
+    const cuuint64_t strides[1] = {256u};
+    const cuuint32_t box[2] = {128u, 1u};  // gather4: one row high
+    const cuuint32_t estr[2] = {1u, 1u};
+    if (!enc || enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        printf("tensor map for gather4 not available\n");
+    } else {
+        run_tma<8, 12>(tmap, idx, n, dout, err, expect);
+        run_tma<4, 24>(tmap, idx, n, dout, err, expect);
+        run_tma<16, 6>(tmap, idx, n, dout, err, expect);
+        run_tma<8, 24>(tmap, idx, n, dout, err, expect);
+        run_tma<16, 12>(tmap, idx, n, dout, err, expect);
+    }
     cudaError_t e = cudaDeviceSynchronize();
     printf("status %s\n", cudaGetErrorString(e));
     return e == cudaSuccess ? 0 : 1;
