@@ -2,13 +2,15 @@
 // pattern of the ROWS SpMM plan, without its sparse bookkeeping). B = 2^24 rows x 128 fp16
 // (4.3 GB); 2^26 row indices drawn uniformly from the first `span` rows (mode 0: all rows,
 // 1: 2^20 rows = 268 MB, 2: 2^17 rows = 34 MB, i.e. L2-resident). Two ways to gather:
-//   * registers: a 16-lane group loads 16 indices coalesced and gathers them in rounds of 8 rows
-//     whose loads are issued together; each lane sums its 16 bytes of each row;
+//   * registers: a 16-lane group loads 16 indices coalesced (one round ahead) and gathers them in
+//     rounds of 8 rows whose loads are issued together; each lane sums its 16 bytes of each row;
 //   * TMA tile::gather4: each warp keeps a ring of kDepth 1-KB slots in shared memory, lane 0
 //     fills a slot with four B rows per instruction (completion on the slot's mbarrier) and the
 //     warp sums the slot, so the rows in flight per SM are set by shared memory, not registers.
 // B holds ((r % 61) + (c % 3)) / 64, so the exact sum of every gathered row is known on the host
-// and the TMA path's result is checked against it. Reports rows/s and gathered TB/s per shape.
+// and the TMA path's result is checked against it. A hybrid CTA runs both kinds of warps on
+// chunks of indices taken from a shared counter, to see whether the two paths add up. Reports
+// rows/s and gathered TB/s per shape.
 //   vcsr_mc_b200/gather_ceiling [mode]
 #include <cuda_fp16.h>
 #include <cuda.h>
@@ -65,8 +67,10 @@ __global__ void __launch_bounds__(WPB * 32) gather16(const uint4* __restrict__ B
             }
         }
     };
+    unsigned nextrow = (p0 + sl < p1) ? __ldcs(idx + p0 + sl) : 0u;
     for (long long p = p0; p < p1; p += 16) {
-        const unsigned myrow = (p + sl < p1) ? __ldcs(idx + p + sl) : 0u;
+        const unsigned myrow = nextrow;  // loaded one round ahead
+        nextrow = (p + 16 + sl < p1) ? __ldcs(idx + p + 16 + sl) : 0u;
         const uint4* a[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) a[k] = B + (size_t)__shfl_sync(gmask, myrow, k, 16) * 16 + sl;
@@ -137,22 +141,33 @@ __global__ void __launch_bounds__(kWarps * 32) gather4_tma(const __grid_constant
         prefetch_tmap(&tmap);
     }
     __syncwarp();
-    uint4 ynext = make_uint4(0, 0, 0, 0);
-    auto issue = [&](int q, uint4 y) {
-        const int s = q % kDepth;
+    // Indices are loaded a batch of 32 slots at a time, one uint4 (four rows) per lane, one batch
+    // ahead of use: ya holds batch q / 32, yb the next one.
+    uint4 ya = lane < nq ? __ldg(idx4 + g0 + lane) : make_uint4(0, 0, 0, 0);
+    uint4 yb = 32 + lane < nq ? __ldg(idx4 + g0 + 32 + lane) : make_uint4(0, 0, 0, 0);
+    auto issue = [&](int j, uint4 y) {
+        const int s = j % kDepth;
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(&bars[s], 1024u);
         tma_gather4_2d(ring + s * 1024, &tmap, &bars[s], 0, int(y.x), int(y.y), int(y.z), int(y.w));
     };
-    const int pre = nq < kDepth ? nq : kDepth;
-    if (lane == 0) {
-        for (int q = 0; q < pre; ++q) issue(q, __ldg(idx4 + g0 + q));
-        if (pre < nq) ynext = __ldg(idx4 + g0 + pre);
+    const int pre = nq < kDepth ? nq : kDepth;  // kDepth <= 32: the first slots are all in batch 0
+    for (int j = 0; j < pre; ++j) {
+        uint4 y;
+        y.x = __shfl_sync(0xffffffffu, ya.x, j);
+        y.y = __shfl_sync(0xffffffffu, ya.y, j);
+        y.z = __shfl_sync(0xffffffffu, ya.z, j);
+        y.w = __shfl_sync(0xffffffffu, ya.w, j);
+        if (lane == 0) issue(j, y);
     }
-    int issued = pre;
     float acc = 0.f;
     int q = 0;
     for (; q < nq; ++q) {
+        if (q > 0 && (q & 31) == 0) {  // entering batch q / 32: shift, and load the one after
+            ya = yb;
+            const int nxt = q + 32 + lane;
+            yb = nxt < nq ? __ldg(idx4 + g0 + nxt) : make_uint4(0, 0, 0, 0);
+        }
         const int s = q % kDepth;
         const bool ok = mbar_wait_bounded(&bars[s], uint32_t(q / kDepth) & 1u);
         if (!__all_sync(0xffffffffu, ok)) break;
@@ -166,13 +181,18 @@ __global__ void __launch_bounds__(kWarps * 32) gather4_tma(const __grid_constant
             acc += (f0.x + f0.y) + (f1.x + f1.y);
         }
         __syncwarp();  // every lane has read slot s before it is refilled
-        if (lane == 0 && issued < nq) {
-            issue(issued, ynext);
-            ++issued;
-            if (issued < nq) ynext = __ldg(idx4 + g0 + issued);
+        const int j = q + kDepth;
+        if (j < nq) {
+            const uint4 from = (j >> 5) == (q >> 5) ? ya : yb;
+            uint4 y;
+            y.x = __shfl_sync(0xffffffffu, from.x, j & 31);
+            y.y = __shfl_sync(0xffffffffu, from.y, j & 31);
+            y.z = __shfl_sync(0xffffffffu, from.z, j & 31);
+            y.w = __shfl_sync(0xffffffffu, from.w, j & 31);
+            if (lane == 0) issue(j, y);
         }
-        issued = __shfl_sync(0xffffffffu, issued, 0);
     }
+    const int issued = q + kDepth < nq ? q + kDepth : nq;
     if (q < nq) {  // a wait expired: let the loads already issued land, then report
         if (lane == 0) {
             for (int r = q; r < issued; ++r) mbar_wait_bounded(&bars[r % kDepth], uint32_t(r / kDepth) & 1u);
@@ -183,6 +203,179 @@ __global__ void __launch_bounds__(kWarps * 32) gather4_tma(const __grid_constant
     double d = acc;
     for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
     if (lane == 0) out[gw] = d;
+}
+
+// Register-gather warps and gather4 warps in one CTA, each warp taking chunks of `chunk` indices
+// from a global counter until none are left. The gather4 warps keep their slot phases across
+// chunks and drain their ring at the end of each chunk. Sums are exact in double.
+template <int kLdgWarps, int kTmaWarps, int kDepth>
+__global__ void __launch_bounds__((kLdgWarps + kTmaWarps) * 32) gather_hybrid(
+    const __grid_constant__ CUtensorMap tmap, const uint4* __restrict__ B, const unsigned* __restrict__ idx, long long n,
+    int chunk, unsigned long long* counter, double* out, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    double total = 0.0;
+    if (warp < kLdgWarps) {
+        const int sub = lane >> 4, sl = lane & 15;
+        const unsigned gmask = 0xffffu << (16 * sub);
+        for (;;) {
+            unsigned long long start = 0;
+            if (lane == 0) start = atomicAdd(counter, (unsigned long long)chunk);
+            start = __shfl_sync(0xffffffffu, start, 0);
+            if ((long long)start >= n) break;
+            const long long c1 = (long long)start + chunk < n ? (long long)start + chunk : n;
+            const long long half = (c1 - (long long)start + 1) / 2;
+            const long long p0 = (long long)start + sub * half;
+            const long long p1 = sub == 0 ? (long long)start + half : c1;
+            float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            unsigned nextrow = (p0 + sl < p1) ? __ldcs(idx + p0 + sl) : 0u;
+            for (long long p = p0; p < p1; p += 16) {  // both halves take the same number of rounds
+                const unsigned myrow = nextrow;
+                nextrow = (p + 16 + sl < p1) ? __ldcs(idx + p + 16 + sl) : 0u;
+                const uint4* a[16];
+                bool v[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    a[k] = B + (size_t)__shfl_sync(gmask, myrow, k, 16) * 16 + sl;
+                    v[k] = p + k < p1;
+                }
+                uint4 r0[8], r1[8];
+                ld8(a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], r0);
+                ld8(a[8], a[9], a[10], a[11], a[12], a[13], a[14], a[15], r1);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    if (!v[k]) continue;
+                    const __half2* h = reinterpret_cast<const __half2*>(k < 8 ? &r0[k] : &r1[k - 8]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 f = __half22float2(h[i]);
+                        acc[2 * i] += f.x;
+                        acc[2 * i + 1] += f.y;
+                    }
+                }
+            }
+            for (int i = 0; i < 8; ++i) total += acc[i];
+        }
+    } else {
+        const int tw = warp - kLdgWarps;
+        uint8_t* ring = smem + tw * kDepth * 1024;
+        uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTmaWarps * kDepth * 1024) + tw * kDepth;
+        if (lane == 0) {
+            for (int s = 0; s < kDepth; ++s) mbar_init(&bars[s], 1);
+            fence_mbar_init();
+        }
+        __syncwarp();
+        const uint4* idx4 = reinterpret_cast<const uint4*>(idx);
+        uint32_t u = 0;  // slots used so far (phase = (u / kDepth) & 1)
+        float acc = 0.f;
+        bool failed = false;
+        for (; !failed;) {
+            unsigned long long start = 0;
+            if (lane == 0) start = atomicAdd(counter, (unsigned long long)chunk);
+            start = __shfl_sync(0xffffffffu, start, 0);
+            if ((long long)start >= n) break;
+            const long long c1 = (long long)start + chunk < n ? (long long)start + chunk : n;
+            const int nq = int((c1 - (long long)start) / 4);  // n and chunk are multiples of 4
+            const long long g0 = (long long)start / 4;
+            uint4 ya = lane < nq ? __ldg(idx4 + g0 + lane) : make_uint4(0, 0, 0, 0);
+            uint4 yb = 32 + lane < nq ? __ldg(idx4 + g0 + 32 + lane) : make_uint4(0, 0, 0, 0);
+            auto issue = [&](int j, const uint4& from) {
+                uint4 y;
+                y.x = __shfl_sync(0xffffffffu, from.x, j & 31);
+                y.y = __shfl_sync(0xffffffffu, from.y, j & 31);
+                y.z = __shfl_sync(0xffffffffu, from.z, j & 31);
+                y.w = __shfl_sync(0xffffffffu, from.w, j & 31);
+                if (lane == 0) {
+                    const int s = int((u + uint32_t(j)) % kDepth);
+                    fence_proxy_async_smem();
+                    mbar_arrive_expect_tx(&bars[s], 1024u);
+                    tma_gather4_2d(ring + s * 1024, &tmap, &bars[s], 0, int(y.x), int(y.y), int(y.z), int(y.w));
+                }
+            };
+            const int pre = nq < kDepth ? nq : kDepth;
+            for (int j = 0; j < pre; ++j) issue(j, ya);
+            int q = 0;
+            for (; q < nq; ++q) {
+                if (q > 0 && (q & 31) == 0) {
+                    ya = yb;
+                    const int nxt = q + 32 + lane;
+                    yb = nxt < nq ? __ldg(idx4 + g0 + nxt) : make_uint4(0, 0, 0, 0);
+                }
+                const uint32_t w = u + uint32_t(q);
+                const int s = int(w % kDepth);
+                const bool ok = mbar_wait_bounded(&bars[s], (w / kDepth) & 1u);
+                if (!__all_sync(0xffffffffu, ok)) break;
+                const uint4* src = reinterpret_cast<const uint4*>(ring + s * 1024) + lane * 2;
+                const uint4 a = src[0], b = src[1];
+                const __half2* h0 = reinterpret_cast<const __half2*>(&a);
+                const __half2* h1 = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f0 = __half22float2(h0[i]), f1 = __half22float2(h1[i]);
+                    acc += (f0.x + f0.y) + (f1.x + f1.y);
+                }
+                __syncwarp();
+                const int j = q + kDepth;
+                if (j < nq) issue(j, (j >> 5) == (q >> 5) ? ya : yb);
+            }
+            if (q < nq) {  // a wait expired: drain what was issued, report, stop
+                const int issued = q + kDepth < nq ? q + kDepth : nq;
+                if (lane == 0) {
+                    for (int r = q; r < issued; ++r) {
+                        const uint32_t w = u + uint32_t(r);
+                        mbar_wait_bounded(&bars[w % kDepth], (w / kDepth) & 1u);
+                    }
+                    atomicOr(err, 1);
+                }
+                failed = true;
+            }
+            u += uint32_t(nq);
+            total += acc;  // acc < 2^18 per chunk: exact in fp32
+            acc = 0.f;
+        }
+    }
+    for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (lane == 0) atomicAdd(out, total);
+}
+
+template <int kLdgWarps, int kTmaWarps, int kDepth>
+void run_hybrid(const CUtensorMap& tmap, const uint4* B, const unsigned* idx, long long n, double* out,
+                unsigned long long* counter, int* err, double expect, int sms) {
+    const int threads = (kLdgWarps + kTmaWarps) * 32;
+    const int smem = kTmaWarps * kDepth * 1024 + kTmaWarps * kDepth * 8 + 1024;
+    auto k = gather_hybrid<kLdgWarps, kTmaWarps, kDepth>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return;
+    int nb = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, threads, smem);
+    if (nb == 0) {
+        printf("hybrid   L=%2d T=%2d D=%2d: does not fit\n", kLdgWarps, kTmaWarps, kDepth);
+        return;
+    }
+    cudaFuncAttributes fa; cudaFuncGetAttributes(&fa, k);
+    const int chunk = 4096;
+    cudaEvent_t a, b; cudaEventCreate(&a); cudaEventCreate(&b);
+    float total_ms = 0.f;
+    double sum = 0.0;
+    const int reps = 6;
+    for (int w = 0; w < reps; ++w) {  // first launch is warm-up
+        cudaMemset(counter, 0, sizeof(unsigned long long));
+        cudaMemset(out, 0, sizeof(double));
+        cudaEventRecord(a);
+        k<<<sms * nb, threads, smem>>>(tmap, B, idx, n, chunk, counter, out, err);
+        cudaEventRecord(b);
+        cudaEventSynchronize(b);
+        float ms; cudaEventElapsedTime(&ms, a, b);
+        if (w > 0) total_ms += ms;
+        cudaMemcpy(&sum, out, sizeof(double), cudaMemcpyDeviceToHost);
+    }
+    int herr = 0;
+    cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost);
+    const float ms = total_ms / (reps - 1);
+    printf("hybrid   L=%2d T=%2d D=%2d regs=%3d CTAs/SM=%d : %.3f ms  %6.2f G rows/s  %.2f TB/s  sum %s%s\n", kLdgWarps,
+           kTmaWarps, kDepth, fa.numRegs, nb, ms, n / (ms * 1e6), n * 256.0 / (ms * 1e9),
+           sum == expect ? "exact" : "WRONG", herr ? " (a wait expired)" : "");
 }
 
 template <int kWarps, int kDepth>
@@ -254,10 +447,18 @@ int main(int argc, char** argv) {
         printf("tensor map for gather4 not available\n");
     } else {
         run_tma<8, 12>(tmap, idx, n, dout, err, expect);
-        run_tma<4, 24>(tmap, idx, n, dout, err, expect);
-        run_tma<16, 6>(tmap, idx, n, dout, err, expect);
-        run_tma<8, 24>(tmap, idx, n, dout, err, expect);
         run_tma<16, 12>(tmap, idx, n, dout, err, expect);
+        run_tma<8, 24>(tmap, idx, n, dout, err, expect);
+        run_tma<16, 6>(tmap, idx, n, dout, err, expect);
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+        unsigned long long* counter;
+        cudaMalloc(&counter, sizeof(unsigned long long));
+        run_hybrid<8, 4, 12>(tmap, B, idx, n, dout, counter, err, expect, sms);
+        run_hybrid<8, 2, 16>(tmap, B, idx, n, dout, counter, err, expect, sms);
+        run_hybrid<16, 8, 12>(tmap, B, idx, n, dout, counter, err, expect, sms);
+        run_hybrid<8, 0, 1>(tmap, B, idx, n, dout, counter, err, expect, sms);
+        run_hybrid<0, 8, 12>(tmap, B, idx, n, dout, counter, err, expect, sms);
     }
     cudaError_t e = cudaDeviceSynchronize();
     printf("status %s\n", cudaGetErrorString(e));
