@@ -32,7 +32,28 @@ namespace vcsrmc {
 namespace dev {
 namespace {
 
-constexpr int kWarpsPerBlock = 8;
+// Build-time shape of vcsr_rows_kernel: warps per block, the minimum resident blocks per SM the
+// register budget is sized for (0: not given; giving 1 already changes the compiler's
+// allocation), B gathers in flight per lane. Gathers in flight per SM decide its speed: on the
+// 2^24-row R-MAT, 4-warp blocks held to 72 registers (7 blocks = 28 warps per SM) run in
+// 9.65 ms against 10.50 ms for 8-warp blocks at 80 registers (24 warps), and 16 gathers in flight
+// per lane at 128 registers (16 warps) in 11.21 ms.
+#ifndef VCSRMC_ROWS_WARPS
+#define VCSRMC_ROWS_WARPS 4
+#endif
+#ifndef VCSRMC_ROWS_MIN_BLOCKS
+#define VCSRMC_ROWS_MIN_BLOCKS 7
+#endif
+#if VCSRMC_ROWS_MIN_BLOCKS > 0
+#define VCSRMC_ROWS_BOUNDS __launch_bounds__(VCSRMC_ROWS_WARPS * 32, VCSRMC_ROWS_MIN_BLOCKS)
+#else
+#define VCSRMC_ROWS_BOUNDS __launch_bounds__(VCSRMC_ROWS_WARPS * 32)
+#endif
+#ifndef VCSRMC_ROWS_IN_FLIGHT
+#define VCSRMC_ROWS_IN_FLIGHT 8
+#endif
+constexpr int kWarpsPerBlock = VCSRMC_ROWS_WARPS;
+constexpr int kFoldedWarpsPerBlock = 8;  // vcsr_rows_folded_kernel (narrow B)
 constexpr unsigned kFull = 0xffffffffu;
 
 // One lane's share of an entry's B row: 16 bytes = 8 fp16 or 4 fp32 consecutive columns.
@@ -136,7 +157,8 @@ __device__ __forceinline__ void write_lane(float* dst, const float (&acc)[8], fl
     }
 }
 
-constexpr int kInFlight = 8;  // B gathers in flight per lane
+constexpr int kInFlight = VCSRMC_ROWS_IN_FLIGHT;  // B gathers in flight per lane
+static_assert(kInFlight == 8 || kInFlight == 16, "a batch of 16 entries in rounds of 8 or 16");
 
 // A lane group (kL lanes: 16 for fp16 B, 32 for fp32 B) owns one work unit and one 128-column
 // slab of C; lane sl of the group holds columns c0 .. c0+kE-1 of it. Per batch of kL entries the
@@ -145,7 +167,7 @@ constexpr int kInFlight = 8;  // B gathers in flight per lane
 // and gathers B eight entries at a time; runs of eight entries without a row end skip the
 // per-entry row-end test.
 template <bool kVec, bool kAccumulate, typename VT, typename BT>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+__global__ void VCSRMC_ROWS_BOUNDS
     vcsr_rows_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
                      const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
                      int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale) {
@@ -257,7 +279,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 // folds sharing a row are contiguous); a row that continues past a step is carried in every
 // lane's accumulator; the fold holding a row's last entry writes the row.
 template <int kF, bool kVec, bool kAccumulate, typename VT, typename BT>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kFoldedWarpsPerBlock * 32)
     vcsr_rows_folded_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
                             const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
                             int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale) {
@@ -269,13 +291,13 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     constexpr int kGroups = 32 / kL;
     constexpr RowOut kOut = kAccumulate ? RowOut::kAdd : RowOut::kStore;
     static_assert(kF == 2 || kF == 4, "fold of 2 or 4 entries");
-    __shared__ int2 stage_all[kWarpsPerBlock * 32];
+    __shared__ int2 stage_all[kFoldedWarpsPerBlock * 32];
     const int lane = threadIdx.x & 31;
     const int sub = lane / kL, sl = lane % kL;
     const int fold = sl / kW, cl = sl % kW;
     const unsigned gmask = kL == 32 ? kFull : (0xffffu << (16 * sub));
     int2* stage = stage_all + (threadIdx.x >> 5) * 32 + sub * kL;
-    const int64_t unit = (int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5)) * kGroups + sub;
+    const int64_t unit = (int64_t(blockIdx.x) * kFoldedWarpsPerBlock + (threadIdx.x >> 5)) * kGroups + sub;
     if (unit >= n_units) return;  // the whole group leaves together
     const int4 u = units[unit];
     const int c0 = kE * cl;  // one slab: O <= kW * kE
@@ -393,17 +415,19 @@ cudaError_t launch_rows_t(const RowPlanView& P, const BT* B, int64_t ldb, int O,
     constexpr int kGroupsPerWarp = 32 / kL;
     const int64_t per_block = int64_t(kWarpsPerBlock) * kGroupsPerWarp;
     const int64_t blocks = (P.n_units + per_block - 1) / per_block;
+    const int64_t per_fblock = int64_t(kFoldedWarpsPerBlock) * kGroupsPerWarp;
+    const int64_t fblocks = (P.n_units + per_fblock - 1) / per_fblock;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
     const int row_bytes = int(ldb * int64_t(sizeof(BT)));
     const VT* vals = static_cast<const VT*>(P.vals);
     // narrow B: fold 4 or 2 entries into one lane group when a row slice fits a quarter or half
     if (O <= kL * kE / 4) {
-        vcsr_rows_folded_kernel<4, kVec, kAcc, VT, BT><<<unsigned(blocks), kWarpsPerBlock * 32, 0, st>>>(
+        vcsr_rows_folded_kernel<4, kVec, kAcc, VT, BT><<<unsigned(fblocks), kFoldedWarpsPerBlock * 32, 0, st>>>(
             P.units, P.n_units, P.rp, P.cols, vals, B, row_bytes, O, C, ldc, P.scale);
         return cudaGetLastError();
     }
     if (O <= kL * kE / 2) {
-        vcsr_rows_folded_kernel<2, kVec, kAcc, VT, BT><<<unsigned(blocks), kWarpsPerBlock * 32, 0, st>>>(
+        vcsr_rows_folded_kernel<2, kVec, kAcc, VT, BT><<<unsigned(fblocks), kFoldedWarpsPerBlock * 32, 0, st>>>(
             P.units, P.n_units, P.rp, P.cols, vals, B, row_bytes, O, C, ldc, P.scale);
         return cudaGetLastError();
     }

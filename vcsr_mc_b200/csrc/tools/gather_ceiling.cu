@@ -11,13 +11,16 @@
 // and the TMA path's result is checked against it. A hybrid CTA runs both kinds of warps on
 // chunks of indices taken from a shared counter, to see whether the two paths add up. Reports
 // rows/s and gathered TB/s per shape.
-//   vcsr_mc_b200/gather_ceiling [mode]
+// Mode 3 gathers a given index stream instead, in its order: an int32 .npy file of row indices
+// below 2^24 (e.g. the column array of a CSR, as the ROWS plan walks it), register gathers only.
+//   vcsr_mc_b200/gather_ceiling [mode] [indices.npy]
 #include <cuda_fp16.h>
 #include <cuda.h>
 #include <cstdio>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <string>
 #include <vector>
 #include <random>
 
@@ -410,25 +413,82 @@ void run_tma(const CUtensorMap& tmap, const unsigned* idx, long long n, double* 
            sum == expect ? "exact" : "WRONG", herr ? " (a wait expired)" : "");
 }
 
+// An int32 (little-endian '<i4') one-dimensional .npy file; false unless every value is in [0, limit).
+bool read_npy_indices(const char* path, long long limit, std::vector<unsigned>& out) {
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return false;
+    unsigned char pre[10];
+    bool ok = std::fread(pre, 1, 10, f) == 10 && std::memcmp(pre, "\x93NUMPY", 6) == 0;
+    long long hlen = 0, hstart = 10;
+    if (ok && pre[6] == 1) {
+        hlen = pre[8] | (pre[9] << 8);
+    } else if (ok && (pre[6] == 2 || pre[6] == 3)) {
+        unsigned char b[2];
+        ok = std::fread(b, 1, 2, f) == 2;
+        hlen = pre[8] | (pre[9] << 8) | ((long long)b[0] << 16) | ((long long)b[1] << 24);
+        hstart = 12;
+    } else {
+        ok = false;
+    }
+    std::string hdr(size_t(ok ? hlen : 0), ' ');
+    ok = ok && std::fread(&hdr[0], 1, size_t(hlen), f) == size_t(hlen) && hdr.find("'<i4'") != std::string::npos &&
+         hdr.find("'fortran_order': False") != std::string::npos;
+    if (ok) {
+        std::fseek(f, 0, SEEK_END);
+        const long long bytes = std::ftell(f) - hstart - hlen;
+        ok = bytes >= 0 && bytes % 4 == 0;
+        if (ok) {
+            out.resize(size_t(bytes / 4));
+            std::fseek(f, long(hstart + hlen), SEEK_SET);
+            ok = std::fread(out.data(), 4, out.size(), f) == out.size();
+        }
+    }
+    std::fclose(f);
+    if (!ok) return false;
+    for (const unsigned x : out)
+        if ((long long)x >= limit) return false;
+    return !out.empty();
+}
+
 int main(int argc, char** argv) {
     const long long nrows = 1LL << 24;  // 16.8M rows x 256 B = 4.3 GB
-    const long long n = 1LL << 26;      // gathers
+    long long n = 1LL << 26;            // gathers
     const int mode = argc > 1 ? atoi(argv[1]) : 0;
+    std::vector<unsigned> given;
+    if (mode == 3) {
+        if (argc < 3 || !read_npy_indices(argv[2], nrows, given)) {
+            printf("mode 3 needs an int32 .npy of indices below %lld\n", nrows);
+            return 1;
+        }
+        n = (long long)given.size();
+    }
     uint4* B; unsigned* idx; float* out; double* dout; int* err;
     if (cudaMalloc(&B, nrows * 256) != cudaSuccess) { printf("oom\n"); return 1; }
     fill_b<<<148 * 16, 256>>>(reinterpret_cast<__half*>(B), nrows);
     cudaMalloc(&idx, n * 4); cudaMalloc(&out, 1 << 24); cudaMalloc(&dout, (n / 4096 + 1) * sizeof(double));
     cudaMalloc(&err, sizeof(int)); cudaMemset(err, 0, sizeof(int));
-    std::vector<unsigned> h(n);
-    std::mt19937_64 rng(1);
-    const long long span = mode == 0 ? nrows : (mode == 1 ? (1LL << 20) : (1LL << 17));
-    double expect = 0;
-    for (auto& x : h) {
-        x = unsigned(rng() % span);
-        expect += 2.0 * (x % 61) + 127.0 / 64.0;  // sum of row x of B
+    std::vector<unsigned> h;
+    if (mode == 3) {
+        h.swap(given);
+        printf("mode 3: %lld given indices from %s\n", n, argv[2]);
+    } else {
+        h.resize(n);
+        std::mt19937_64 rng(1);
+        const long long span = mode == 0 ? nrows : (mode == 1 ? (1LL << 20) : (1LL << 17));
+        for (auto& x : h) x = unsigned(rng() % span);
+        printf("mode %d: rows uniform over %lld (%.0f MB)\n", mode, span, span * 256.0 / 1e6);
     }
+    double expect = 0;
+    for (const unsigned x : h) expect += 2.0 * (x % 61) + 127.0 / 64.0;  // sum of row x of B
     cudaMemcpy(idx, h.data(), n * 4, cudaMemcpyHostToDevice);
-    printf("mode %d: rows uniform over %lld (%.0f MB)\n", mode, span, span * 256.0 / 1e6);
+    if (mode == 3) {
+        run<8, true>(B, idx, n, out, "double");
+        run<4, true>(B, idx, n, out, "double");
+        run<8, false>(B, idx, n, out, "single");
+        cudaError_t e = cudaDeviceSynchronize();
+        printf("status %s\n", cudaGetErrorString(e));
+        return e == cudaSuccess ? 0 : 1;
+    }
     run<8, false>(B, idx, n, out, "single");
     run<8, true>(B, idx, n, out, "double");
     run<4, true>(B, idx, n, out, "double");
