@@ -47,10 +47,13 @@ __device__ __forceinline__ void ld8(const uint4* p0, const uint4* p1, const uint
         : "l"(p0), "l"(p1), "l"(p2), "l"(p3), "l"(p4), "l"(p5), "l"(p6), "l"(p7));
 }
 
-// R rounds of 8 per batch of 16 indices; kDouble: issue round r+1 before consuming round r
-template <int WPB, bool kDouble>
+// R rounds of 8 per batch of 16 indices; kDouble: issue round r+1 before consuming round r.
+// kWriteRows: after each batch of 16 the group also stores its 16 x 8 fp32 sums as one 512-byte
+// row of `rows_out` (row p / 16, streaming stores), the C stream of the SpMM.
+template <int WPB, bool kDouble, bool kWriteRows = false>
 __global__ void __launch_bounds__(WPB * 32) gather16(const uint4* __restrict__ B, const unsigned* __restrict__ idx,
-                                                     long long n, float* __restrict__ out, int per_group) {
+                                                     long long n, float* __restrict__ out, int per_group,
+                                                     float* __restrict__ rows_out = nullptr) {
     const int lane = threadIdx.x & 31, sub = lane >> 4, sl = lane & 15;
     const unsigned gmask = 0xffffu << (16 * sub);
     const long long g = (long long)(blockIdx.x * WPB + (threadIdx.x >> 5)) * 2 + sub;
@@ -88,6 +91,13 @@ __global__ void __launch_bounds__(WPB * 32) gather16(const uint4* __restrict__ B
             ld8(a[8], a[9], a[10], a[11], a[12], a[13], a[14], a[15], r1);
             consume(r1);
         }
+        if (kWriteRows) {
+            float4* dst = reinterpret_cast<float4*>(rows_out + (size_t)(p >> 4) * 128 + sl * 8);
+            __stcs(dst, make_float4(acc[0], acc[1], acc[2], acc[3]));
+            __stcs(dst + 1, make_float4(acc[4], acc[5], acc[6], acc[7]));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        }
     }
     float s = 0;
 #pragma unroll
@@ -95,20 +105,21 @@ __global__ void __launch_bounds__(WPB * 32) gather16(const uint4* __restrict__ B
     if (s == 12345.f) out[g] = s;  // keep the loads alive
 }
 
-template <int WPB, bool kDouble>
-void run(const uint4* B, const unsigned* idx, long long n, float* out, const char* name) {
+template <int WPB, bool kDouble, bool kWriteRows = false>
+void run(const uint4* B, const unsigned* idx, long long n, float* out, const char* name, float* rows_out = nullptr) {
     const int per_group = 256;
     const long long groups = (n + per_group - 1) / per_group;
     const long long blocks = (groups + 2 * WPB - 1) / (2 * WPB);
+    auto k = gather16<WPB, kDouble, kWriteRows>;
     cudaEvent_t a, b; cudaEventCreate(&a); cudaEventCreate(&b);
-    for (int w = 0; w < 2; ++w) gather16<WPB, kDouble><<<blocks, WPB * 32>>>(B, idx, n, out, per_group);
+    for (int w = 0; w < 2; ++w) k<<<blocks, WPB * 32>>>(B, idx, n, out, per_group, rows_out);
     cudaEventRecord(a);
     const int reps = 5;
-    for (int w = 0; w < reps; ++w) gather16<WPB, kDouble><<<blocks, WPB * 32>>>(B, idx, n, out, per_group);
+    for (int w = 0; w < reps; ++w) k<<<blocks, WPB * 32>>>(B, idx, n, out, per_group, rows_out);
     cudaEventRecord(b); cudaEventSynchronize(b);
     float ms; cudaEventElapsedTime(&ms, a, b);
-    int nb = 0; cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gather16<WPB, kDouble>, WPB * 32, 0);
-    cudaFuncAttributes fa; cudaFuncGetAttributes(&fa, gather16<WPB, kDouble>);
+    int nb = 0; cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, WPB * 32, 0);
+    cudaFuncAttributes fa; cudaFuncGetAttributes(&fa, k);
     ms /= reps;
     printf("%-8s WPB=%2d regs=%3d warps/SM=%2d : %.3f ms  %6.2f G rows/s  %.2f TB/s\n", name, WPB, fa.numRegs, nb * WPB, ms,
            n / (ms * 1e6), n * 256.0 / (ms * 1e9));
@@ -485,6 +496,18 @@ int main(int argc, char** argv) {
         run<8, true>(B, idx, n, out, "double");
         run<4, true>(B, idx, n, out, "double");
         run<8, false>(B, idx, n, out, "single");
+        // the same gathers plus one 512-byte fp32 row stored per 16 entries (a C stream)
+        float* rows_out = nullptr;
+        const long long nrows_out = (n + 15) / 16;
+        if (cudaMalloc(&rows_out, nrows_out * 512) == cudaSuccess) {
+            printf("with a 512-byte row stored per 16 gathers (%.2f GB written):\n", nrows_out * 512.0 / 1e9);
+            run<4, true, true>(B, idx, n, out, "double+C", rows_out);
+            run<8, false, true>(B, idx, n, out, "single+C", rows_out);
+            cudaFree(rows_out);
+        } else {
+            cudaGetLastError();
+            printf("no room for the row stream\n");
+        }
         cudaError_t e = cudaDeviceSynchronize();
         printf("status %s\n", cudaGetErrorString(e));
         return e == cudaSuccess ? 0 : 1;
