@@ -581,10 +581,10 @@ def main() -> None:
                "pipelining": "upload of step i+1 overlaps download of step i (two device buffers, two copy streams)",
                "steps": args.e2e_steps,
                "link": {"h2d_ms": up_ms, "d2h_ms": down_ms, "both_ms": both_ms,
-                        "h2d_GBps": hB.numel() * hB.element_size() / (up_ms * 1e-3) / 1e9,
-                        "d2h_GBps": hC.numel() * hC.element_size() / (down_ms * 1e-3) / 1e9,
+                        "h2d_GBps": hB.numel() * hB.element_size() / (max(up_ms, 1e-6) * 1e-3) / 1e9,
+                        "d2h_GBps": hC.numel() * hC.element_size() / (max(down_ms, 1e-6) * 1e-3) / 1e9,
                         "floor_ms_per_step": both_ms,
-                        "frac": both_ms / float(e2e_ms),
+                        "frac": both_ms / max(float(e2e_ms), 1e-6),
                         "how": "this step's H2D and D2H copies timed alone and at once, max over ranks"},
                "b_staging": ("each rank uploads 1/N of B, NCCL all-gather over NVLink" if world > 1 else
                              "B uploaded whole")}
