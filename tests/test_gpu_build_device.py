@@ -185,3 +185,24 @@ def test_device_build_rejects_unsorted_rows_and_bad_row_ptr(cuda):
     with pytest.raises(vm.VcsrmcError) as e:
         vm.build_vcsr_mc_device(rp, torch.tensor([0, 1, 9], dtype=torch.int32, device="cuda"), val, 2, 8)  # col >= N
     assert e.value.status == 1
+
+
+def test_device_build_rejects_bad_band_requests(cuda):
+    """BAND needs the FP16 format and a band height in [0, 128]; both are argument errors,
+    reported before any device work."""
+    torch = cuda
+    rp = torch.tensor([0, 1, 2], dtype=torch.int32, device="cuda")
+    col = torch.tensor([0, 1], dtype=torch.int32, device="cuda")
+    val = torch.ones(2, dtype=torch.float32, device="cuda")
+    with pytest.raises(vm.VcsrmcError) as e:
+        vm.build_vcsr_mc_device(rp, col, val, 2, 8, fp32=True, plans=[vm.PLAN_BAND])
+    assert e.value.status == 1 and "FP16" in str(e.value)
+    for H in (-1, 129):
+        with pytest.raises(vm.VcsrmcError) as e:
+            vm.build_vcsr_mc_device(rp, col, val, 2, 8, plans=[vm.PLAN_BAND], band_rows=H)
+        assert e.value.status == 1
+    dV = vm.build_vcsr_mc_device(rp, col, val, 2, 8, plans=[vm.PLAN_BAND], band_rows=1)
+    info = dV.info()
+    assert info["plans"] == [vm.PLAN_BAND] and info["band_rows"] == 1 and info["n_bands"] == 2
+    assert info["n_tiles"] == 2 and info["band_cols"] in (32, 64)
+    dV.free()
