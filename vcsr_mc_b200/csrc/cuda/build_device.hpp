@@ -70,7 +70,7 @@ RowsLayout build_rows_layout(const int* row_ptr, const int* col, const float* va
 BandChoice choose_band_device(const int* row_ptr, const int* col, int M, cudaStream_t st);
 
 // The BAND plan's view, bit for bit the one build_band_view makes on the host: a stable segmented
-// sort of each band's entries by column, then one warp per band cuts the greedy 32-column tiles.
+// sort of each band's entries by column, then one warp per band cuts the greedy kBandK-column tiles.
 // Checks the view before returning; throws StatusError on failure (nothing is leaked).
 BandLayout build_band_layout(const int* row_ptr, const int* col, const float* val, int M, int64_t nnz, float scale,
                              int band_rows, cudaStream_t st);
