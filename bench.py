@@ -205,9 +205,28 @@ def time_reference_cpu(M, N, rp, col, val, steps: int, warmup: int, target_nnz: 
         runner.run()
     dt = (time.perf_counter() - t) / max(1, steps)
     runner.close()
+    # the same loop on one core, one pass after one warm-up pass
+    one = ob.RefSpmm(srp, scol, sval, Bs, nslices=1)
+    one.run()
+    t = time.perf_counter()
+    one.run()
+    dt1 = time.perf_counter() - t
+    one.close()
     return {"value": 2.0 * snnz * O_COLS / dt / 1e9, "unit": "GFLOP/s", "cores": cores, "kind": "reference",
             "sample": desc + f"; reference loop src/main.cpp:202-207 on {cores} row slices/threads",
-            "ms_per_step": dt * 1e3}
+            "ms_per_step": dt * 1e3, "cpu_model": cpu_model(),
+            "single_core": {"value": 2.0 * snnz * O_COLS / dt1 / 1e9, "unit": "GFLOP/s", "ms_per_step": dt1 * 1e3}}
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def time_cusparse(rp, col, val, r0, r1, p0, p1, N, B, fp16: bool, stream) -> dict:
@@ -353,7 +372,7 @@ def main() -> None:
             "unit": "GFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f64" , "data": "synthetic", "config": config,
-            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model", "single_core")},
             "e2e": {"value": cb["value"], "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return
 
@@ -632,7 +651,7 @@ def main() -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             cb = time_reference_cpu(M, N, rp, col, val, 3, 1, args.cpu_sample_nnz, fp16)
-            cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model", "single_core")}
         except Exception as e:  # noqa: BLE001
             cpu = {"value": None, "unavailable": f"{type(e).__name__}: {e}"}
 
