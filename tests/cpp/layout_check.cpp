@@ -1,0 +1,227 @@
+// Host-side layout builders of the ROWS and BAND plans, checked on the CPU (no GPU involved):
+// pack_units (the work units of the row view) and build_band_view / choose_band (the BAND view).
+// Each rule is stated here as properties of the output, not re-run: heavy rows become
+// unit_nnz-entry chunks listed first; light rows form maximal greedy runs of at most kUnitRows rows
+// and unit_nnz entries; the BAND view holds exactly each band's entries, in (column, row) order,
+// in tiles whose starts are the greedy starts over the band's sorted columns.
+// Linked against the library's own objects (vcsr_mc_b200/_build/cuda/plan_rows.o, plan_band.o) by
+// tests/test_layouts_cpu.py. Prints "OK ..." and exits 0, or names the first failed check.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <random>
+#include <set>
+#include <tuple>
+#include <vector>
+
+#include "cuda/plan_band.hpp"
+#include "cuda/plan_rows.hpp"
+
+using namespace vcsrmc::dev;
+
+namespace {
+
+using ll = long long;
+int failures = 0;
+ll densest_tile = 0;
+void expect(bool ok, const char* what, long long a = 0, long long b = 0) {
+    if (!ok && failures++ < 5) std::printf("FAIL %s (%lld, %lld)\n", what, a, b);
+}
+
+struct Csr {
+    int M = 0, N = 0;
+    std::vector<int> rp, col;
+    std::vector<float> val;
+};
+
+// Row lengths from `draw`, columns sorted and distinct in [0, N), values U(-2, 2).
+template <class Draw>
+Csr make_csr(int M, int N, std::mt19937_64& g, Draw draw) {
+    Csr a;
+    a.M = M;
+    a.N = N;
+    a.rp.assign(size_t(M) + 1, 0);
+    std::uniform_real_distribution<float> uv(-2.f, 2.f);
+    for (int r = 0; r < M; ++r) {
+        std::set<int> cs;
+        const int len = std::min(N, draw(r));
+        std::uniform_int_distribution<int> uc(0, N - 1);
+        while (int(cs.size()) < len) cs.insert(uc(g));
+        for (int c : cs) {
+            a.col.push_back(c);
+            a.val.push_back(uv(g));
+        }
+        a.rp[size_t(r) + 1] = int(a.col.size());
+    }
+    return a;
+}
+
+// A banded matrix like a 3-D stencil: row r holds columns r + d for d in three windows of three
+// (offsets 0, +-w, +-w*w with w = 10), clipped to [0, M), plus an occasional random column.
+Csr make_banded(int M, std::mt19937_64& g) {
+    Csr a;
+    a.M = a.N = M;
+    a.rp.assign(size_t(M) + 1, 0);
+    std::uniform_real_distribution<float> uv(-2.f, 2.f);
+    std::uniform_int_distribution<int> uc(0, M - 1);
+    for (int r = 0; r < M; ++r) {
+        std::set<int> cs;
+        for (int plane : {-100, 0, 100})
+            for (int line : {-10, 0, 10})
+                for (int d : {-1, 0, 1}) {
+                    const int c = r + plane + line + d;
+                    if (c >= 0 && c < M) cs.insert(c);
+                }
+        if (g() % 8 == 0) cs.insert(uc(g));
+        for (int c : cs) {
+            a.col.push_back(c);
+            a.val.push_back(uv(g));
+        }
+        a.rp[size_t(r) + 1] = int(a.col.size());
+    }
+    return a;
+}
+
+void check_units(const std::vector<int>& rp, int M, int u) {
+    std::vector<RowViewHost::Unit> units;
+    std::vector<int> split;
+    pack_units(rp.data(), M, u, units, split);
+    auto len = [&](int r) { return rp[size_t(r) + 1] - rp[size_t(r)]; };
+    size_t k = 0;
+    std::vector<int> heavy;
+    for (int r = 0; r < M; ++r)
+        if (len(r) > u) heavy.push_back(r);
+    expect(split == heavy, "split_rows are exactly the rows longer than unit_nnz", ll(split.size()), ll(heavy.size()));
+    for (int r : heavy)  // chunks of the heavy rows first, in row order
+        for (int p = rp[size_t(r)]; p < rp[size_t(r) + 1]; p += u, ++k) {
+            const bool ok = k < units.size() && units[k].x == r && units[k].y == int(unsigned(r + 1) | 0x80000000u) &&
+                            units[k].z == p && units[k].w == std::min(rp[size_t(r) + 1], p + u);
+            expect(ok, "heavy-row chunk", r, p);
+        }
+    int next = 0;  // first row not yet covered by a light run
+    for (; k < units.size(); ++k) {
+        const auto& t = units[k];
+        while (next < M && len(next) > u) ++next;
+        expect(t.x == next, "light run starts at the first uncovered light row", t.x, next);
+        expect(t.y > t.x && t.y - t.x <= kUnitRows && t.y <= M, "light run of 1 .. kUnitRows rows", t.x, t.y);
+        expect(t.z == rp[size_t(t.x)] && t.w == rp[size_t(t.y)], "light run entry range", t.z, t.w);
+        int n = 0;
+        for (int r = t.x; r < t.y; ++r) {
+            expect(len(r) <= u, "light run holds only light rows", r, len(r));
+            n += len(r);
+        }
+        expect(n <= u, "light run within unit_nnz entries", n, u);
+        if (t.y < M && t.y - t.x < kUnitRows && len(t.y) <= u)
+            expect(n + len(t.y) > u, "light run is maximal", t.y, n);
+        next = t.y;
+    }
+    while (next < M && len(next) > u) ++next;
+    expect(next == M, "light runs cover every light row", next, M);
+}
+
+unsigned short half_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
+
+void check_band(const Csr& a, int H) {
+    RowViewHost rv;
+    rv.rp = a.rp;
+    rv.cols = a.col;
+    rv.vals = a.val;
+    const BandViewHost b = build_band_view(rv, a.M, H, 2);
+    const int nb = (a.M + H - 1) / H;
+    expect(int(b.tile_ptr.size()) == nb + 1 && b.tile_ptr[0] == 0, "tile_ptr size", ll(b.tile_ptr.size()), nb + 1);
+    const int T = b.tile_ptr[size_t(nb)];
+    expect(int(b.tile_col.size()) == T && int(b.tile_eptr.size()) == T + 1, "tile arrays", T, ll(b.tile_col.size()));
+    expect(b.ents.size() == a.col.size() && b.tile_eptr[size_t(T)] == int(a.col.size()), "entries", ll(b.ents.size()),
+           ll(a.col.size()));
+    for (int band = 0; band < nb; ++band) {
+        const int r0 = band * H, r1 = std::min(a.M, r0 + H);
+        const int t0 = b.tile_ptr[size_t(band)], t1 = b.tile_ptr[size_t(band) + 1];
+        expect(t1 >= t0, "tile_ptr non-decreasing", band, t1 - t0);
+        // the band's entries as (column, row, fp16 bits), and its greedy tile starts
+        std::vector<std::tuple<int, int, int>> want;
+        for (int r = r0; r < r1; ++r)
+            for (int p = a.rp[size_t(r)]; p < a.rp[size_t(r) + 1]; ++p)
+                want.emplace_back(a.col[size_t(p)], r, half_bits(a.val[size_t(p)]));
+        std::sort(want.begin(), want.end());
+        std::vector<int> starts;
+        long long end = -1;
+        for (const auto& w : want)
+            if (std::get<0>(w) >= end) {
+                starts.push_back(std::get<0>(w));
+                end = std::get<0>(w) + (long long)kBandK;
+            }
+        expect(int(starts.size()) == t1 - t0, "tile count = greedy count", band, ll(starts.size()));
+        if (want.empty()) continue;
+        expect(b.tile_eptr[size_t(t0)] == a.rp[size_t(r0)] && b.tile_eptr[size_t(t1)] == a.rp[size_t(r1)],
+               "band's tiles cover exactly its entries", band, 0);
+        std::vector<std::tuple<int, int, int>> got;
+        for (int t = t0; t < t1; ++t) {
+            if (t - t0 < int(starts.size())) expect(b.tile_col[size_t(t)] == starts[size_t(t - t0)], "tile start", t, b.tile_col[size_t(t)]);
+            expect(b.tile_eptr[size_t(t) + 1] > b.tile_eptr[size_t(t)], "tile not empty", t, 0);
+            densest_tile = std::max<ll>(densest_tile, b.tile_eptr[size_t(t) + 1] - b.tile_eptr[size_t(t)]);
+            for (int e = b.tile_eptr[size_t(t)]; e < b.tile_eptr[size_t(t) + 1]; ++e) {
+                const uint32_t w = b.ents[size_t(e)];
+                const int lc = int(w & uint32_t(kBandK - 1)), row = int((w >> kBandColBits) & 127u);
+                expect(((w >> (kBandColBits + 7)) & ((1u << (16 - kBandColBits - 7)) - 1u)) == 0u, "unused entry bits", e, w);
+                expect(row < r1 - r0, "row within band", e, row);
+                got.emplace_back(b.tile_col[size_t(t)] + lc, r0 + row, int(w >> 16));
+            }
+        }
+        expect(got == want, "band entries in (column, row) order with their fp16 values", band, ll(got.size()));
+    }
+}
+
+}  // namespace
+
+int main() {
+    std::mt19937_64 g(20260923);
+    long long n_units_checked = 0, n_bands_checked = 0;
+    // work units: short, empty, exactly-unit_nnz and heavy rows
+    for (int trial = 0; trial < 40; ++trial) {
+        const int M = trial == 0 ? 0 : (trial == 1 ? 1 : 1 + int(g() % 3000));
+        std::vector<int> rp(size_t(M) + 1, 0);
+        for (int r = 0; r < M; ++r) {
+            const int kind = int(g() % 20);
+            const int len = kind < 6 ? 0 : kind < 16 ? int(g() % 20) : kind < 18 ? 16 << (g() % 7) : int(g() % 5000);
+            rp[size_t(r) + 1] = rp[size_t(r)] + len;
+        }
+        for (int u : {16, 64, 256, 1024}) {
+            check_units(rp, M, u);
+            ++n_units_checked;
+        }
+    }
+    // BAND view: random and banded matrices, several heights, narrow N, empty rows
+    for (int trial = 0; trial < 24; ++trial) {
+        Csr a;
+        if (trial % 3 == 0) {
+            a = make_banded(1 + int(g() % 1500), g);
+        } else {
+            const int M = 1 + int(g() % 500), N = trial % 3 == 1 ? 1 + int(g() % 70) : 1 + int(g() % 5000);
+            a = make_csr(M, N, g, [&](int) { return int(g() % 5) == 0 ? 0 : int(g() % 40); });
+        }
+        for (int H : {1, 37, 64, 112, 128}) {
+            check_band(a, H);
+            ++n_bands_checked;
+        }
+        RowViewHost rv;
+        rv.rp = a.rp;
+        rv.cols = a.col;
+        rv.vals = a.val;
+        const BandChoice c = choose_band(rv, a.M);
+        const std::set<int> cand = {128, 127, 126, 124, 120, 112, 96, 64};
+        expect(cand.count(c.band_rows) == 1, "chosen band height is a candidate", c.band_rows, 0);
+        expect(a.col.empty() || c.entries_per_tile >= 1.0, "entries per tile", trial, 0);
+    }
+    Csr empty;  // M = 0
+    empty.rp = {0};
+    check_band(empty, 128);
+    if (failures) {
+        std::printf("%d checks failed\n", failures);
+        return 1;
+    }
+    std::printf("OK unit_sets=%lld band_views=%lld tile_width=%d densest_tile=%lld\n", n_units_checked, n_bands_checked,
+                kBandK, densest_tile);
+    return 0;
+}
