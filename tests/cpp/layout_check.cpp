@@ -1,11 +1,14 @@
 // Host-side layout builders of the ROWS and BAND plans, checked on the CPU (no GPU involved):
-// pack_units (the work units of the row view) and build_band_view / choose_band (the BAND view).
+// build_row_view (a host-built format transposed back into rows) and pack_units (its work units),
+// build_band_view / choose_band (the BAND view).
 // Each rule is stated here as properties of the output, not re-run: heavy rows become
 // unit_nnz-entry chunks listed first; light rows form maximal greedy runs of at most kUnitRows rows
 // and unit_nnz entries; the BAND view holds exactly each band's entries, in (column, row) order,
 // in tiles whose starts are the greedy starts over the band's sorted columns.
-// Linked against the library's own objects (vcsr_mc_b200/_build/cuda/plan_rows.o, plan_band.o) by
-// tests/test_layouts_cpu.py. Prints "OK ..." and exits 0, or names the first failed check.
+// A row view is the CSR itself (a row with ascending columns lists its entries in the format's
+// order) with the format's work units.
+// Linked against the library's own objects (vcsr_mc_b200/_build/cuda/plan_rows.o, plan_band.o) and
+// libvcsrmc.so (csr_to_vcsr_mc) by tests/test_layouts_cpu.py. Prints "OK ..." and exits 0, or names the first failed check.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -18,6 +21,8 @@
 
 #include "cuda/plan_band.hpp"
 #include "cuda/plan_rows.hpp"
+#include "vcsrmc/csr.hpp"
+#include "vcsrmc/vcsr_formats.hpp"
 
 using namespace vcsrmc::dev;
 
@@ -121,6 +126,30 @@ void check_units(const std::vector<int>& rp, int M, int u) {
     expect(next == M, "light runs cover every light row", next, M);
 }
 
+void check_row_view(const Csr& a, bool fp32, int segw, int u) {
+    vcsrmc::CSR c;
+    c.M = a.M;
+    c.N = a.N;
+    c.nnz = int(a.col.size());
+    c.row_ptr = a.rp;
+    c.col = a.col;
+    c.val = a.val;
+    const vcsrmc::VCSRMC v = vcsrmc::csr_to_vcsr_mc(c, fp32, segw, 2);
+    expect(v.scale == 1.0f, "values in (-2, 2) keep half_scale at 1", 0, 0);
+    const RowViewHost rv = build_row_view(v, u);
+    expect(rv.rp == a.rp, "row view row_ptr is the CSR's", a.M, segw);
+    expect(rv.cols == a.col, "row view columns are the CSR's, in order", a.M, segw);
+    expect(rv.vals == a.val, "row view values are the CSR's", a.M, segw);
+    std::vector<RowViewHost::Unit> units;
+    std::vector<int> split;
+    pack_units(a.rp.data(), a.M, u, units, split);
+    bool same = units.size() == rv.units.size() && split == rv.split_rows;
+    for (size_t i = 0; same && i < units.size(); ++i)
+        same = units[i].x == rv.units[i].x && units[i].y == rv.units[i].y && units[i].z == rv.units[i].z &&
+               units[i].w == rv.units[i].w;
+    expect(same, "row view units are pack_units of its row_ptr", a.M, u);
+}
+
 unsigned short half_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
 
 void check_band(const Csr& a, int H) {
@@ -177,7 +206,7 @@ void check_band(const Csr& a, int H) {
 
 int main() {
     std::mt19937_64 g(20260923);
-    long long n_units_checked = 0, n_bands_checked = 0;
+    long long n_units_checked = 0, n_bands_checked = 0, n_row_views = 0;
     // work units: short, empty, exactly-unit_nnz and heavy rows
     for (int trial = 0; trial < 40; ++trial) {
         const int M = trial == 0 ? 0 : (trial == 1 ? 1 : 1 + int(g() % 3000));
@@ -205,6 +234,8 @@ int main() {
             check_band(a, H);
             ++n_bands_checked;
         }
+        check_row_view(a, trial % 2 == 0, trial % 4 < 2 ? 16 : 32, trial % 3 == 0 ? 64 : 16);
+        ++n_row_views;
         RowViewHost rv;
         rv.rp = a.rp;
         rv.cols = a.col;
@@ -221,7 +252,7 @@ int main() {
         std::printf("%d checks failed\n", failures);
         return 1;
     }
-    std::printf("OK unit_sets=%lld band_views=%lld tile_width=%d densest_tile=%lld\n", n_units_checked, n_bands_checked,
-                kBandK, densest_tile);
+    std::printf("OK unit_sets=%lld band_views=%lld row_views=%lld tile_width=%d densest_tile=%lld\n", n_units_checked,
+                n_bands_checked, n_row_views, kBandK, densest_tile);
     return 0;
 }
