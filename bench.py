@@ -39,7 +39,7 @@ if ROOT not in sys.path:
 O_COLS = 128
 L2_BYTES = 126 * (1 << 20)
 SEED = 0
-# Generated CSRs are cached inside the checkout (git- and gpurun-ignored) so that every rank of a
+# Generated CSRs are cached inside the checkout (a git-ignored folder) so that every rank of a
 # multi-GPU run, and later runs, load the same matrix instead of generating it again.
 CACHE_DIR = os.environ.get("VCSRMC_BENCH_CACHE", os.path.join(ROOT, ".bench_cache"))
 
@@ -166,9 +166,23 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------------
 # CPU baselines (the reference's own fp64 CSR loop, src/main.cpp:202-207, from oracle/_ref)
 # ---------------------------------------------------------------------------------------------
-def cpu_sample(M, N, rp, col, val, target_nnz: int):
-    """Every k-th row of A (k chosen for ~target_nnz), columns compacted to the rows of B they
-    touch. Returns (row_ptr, col, val, B_compact, description)."""
+def mem_available_bytes() -> int:
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) * 1024
+    except (OSError, ValueError, IndexError):
+        pass
+    return 0
+
+
+def cpu_sample(M, N, rp, col, val, target_nnz: int, fp16_b: bool):
+    """Every k-th row of A (k chosen for ~target_nnz), with the full N x O fp32 B holding the GPU
+    run's values (rounded to fp16 on the FP16 path), so that the CPU gathers B rows over the same
+    address span as the whole job. Only when host memory cannot hold four copies of B are the
+    columns compacted to the rows of B the sample touches. Returns (row_ptr, col, val, B,
+    description, nnz)."""
     nnz = int(rp[M])
     k = max(1, int(round(nnz / max(1, target_nnz))))
     rows = np.arange(0, M, k, dtype=np.int64)
@@ -179,23 +193,34 @@ def cpu_sample(M, N, rp, col, val, target_nnz: int):
     idx = np.repeat(starts - srp[:-1], lens) + np.arange(srp[-1])
     scol = np.asarray(col)[idx]
     sval = np.asarray(val)[idx].astype(np.float32)
-    uniq, inv = np.unique(scol, return_inverse=True)
-    from vcsr_mc_b200 import rng
-    Bfull_rows = np.empty((uniq.size, O_COLS), dtype=np.float32)
-    for s in range(0, uniq.size, 1 << 16):  # rows of the dense stream = the GPU's B values
-        Bfull_rows[s:s + (1 << 16)] = rng.dense_rows(uniq[s:s + (1 << 16)], O_COLS, SEED)
-    desc = (f"every {k}-th row of A ({rows.size} rows, {int(srp[-1])} nnz), B compacted to the "
-            f"{uniq.size} rows those touch, fp32, O={O_COLS}")
-    return srp.astype(np.int32), inv.astype(np.int32), sval, Bfull_rows, desc, int(srp[-1])
+    full_bytes = N * O_COLS * 4
+    if mem_available_bytes() > 4 * full_bytes:
+        import vcsr_mc_b200 as vm
+        Bs = vm.gen_dense_host(N, O_COLS, SEED)  # the same stream as the GPU's B
+        if fp16_b:
+            for s in range(0, N, 1 << 20):
+                Bs[s:s + (1 << 20)] = Bs[s:s + (1 << 20)].astype(np.float16).astype(np.float32)
+        bdesc = f"the full {N} x {O_COLS} fp32 B"
+        out_col = scol.astype(np.int32)
+    else:
+        uniq, inv = np.unique(scol, return_inverse=True)
+        from vcsr_mc_b200 import rng
+        Bs = np.empty((uniq.size, O_COLS), dtype=np.float32)
+        for s in range(0, uniq.size, 1 << 16):  # rows of the dense stream = the GPU's B values
+            Bs[s:s + (1 << 16)] = rng.dense_rows(uniq[s:s + (1 << 16)], O_COLS, SEED)
+        if fp16_b:
+            Bs = Bs.astype(np.float16).astype(np.float32)
+        bdesc = f"B compacted to the {uniq.size} rows those touch (host memory too small for the full B), fp32"
+        out_col = inv.astype(np.int32)
+    desc = f"every {k}-th row of A ({rows.size} rows, {int(srp[-1])} nnz), {bdesc}, O={O_COLS}"
+    return srp.astype(np.int32), out_col, sval, Bs, desc, int(srp[-1])
 
 
 def time_reference_cpu(M, N, rp, col, val, steps: int, warmup: int, target_nnz: int, fp16_b: bool):
     from oracle import bind as ob
     if not ob.ref_available():
         raise RuntimeError("oracle/_ref/libvcsr_ref.so not built")
-    srp, scol, sval, Bs, desc, snnz = cpu_sample(M, N, rp, col, val, target_nnz)
-    if fp16_b:
-        Bs = Bs.astype(np.float16).astype(np.float32)
+    srp, scol, sval, Bs, desc, snnz = cpu_sample(M, N, rp, col, val, target_nnz, fp16_b)
     cores = len(os.sched_getaffinity(0))
     runner = ob.RefSpmm(srp, scol, sval, Bs, nslices=cores)
     for _ in range(warmup):
@@ -213,7 +238,8 @@ def time_reference_cpu(M, N, rp, col, val, steps: int, warmup: int, target_nnz: 
     dt1 = time.perf_counter() - t
     one.close()
     return {"value": 2.0 * snnz * O_COLS / dt / 1e9, "unit": "GFLOP/s", "cores": cores, "kind": "reference",
-            "sample": desc + f"; reference loop src/main.cpp:202-207 on {cores} row slices/threads",
+            "sample": desc + f"; reference loop src/main.cpp:202-207 on {cores} row slices/threads, "
+                             f"{steps} timed passes after {warmup} warm-up",
             "ms_per_step": dt * 1e3, "cpu_model": cpu_model(),
             "single_core": {"value": 2.0 * snnz * O_COLS / dt1 / 1e9, "unit": "GFLOP/s", "ms_per_step": dt1 * 1e3}}
 
@@ -324,19 +350,24 @@ def main() -> None:
     ap.add_argument("--no-cusparse", action="store_true")
     ap.add_argument("--no-c-gather", action="store_true", help="skip the separately timed gather of C to rank 0 (N > 1)")
     ap.add_argument("--cpu-sample-nnz", type=int, default=8_000_000)
-    ap.add_argument("--build", choices=["host", "device"], default="host",
-                    help="format construction: host (bit-identical to the reference builder) or device (GPU)")
+    ap.add_argument("--build", choices=["host", "device"], default="device",
+                    help="format construction: device (GPU builder, about 0.3 s on config 4) or host (bit-identical "
+                         "to the reference builder, about 15 s on config 4 and all host cores per rank)")
     ap.add_argument("--unit-nnz", type=int, default=0,
                     help="ROWS plan: entries per work unit (0 = the library's choice for the matrix)")
-    ap.add_argument("--row-weight", type=float, default=5.4,
-                    help="shard balance: cost = nnz + row_weight * rows (0 = nnz balance)")
+    ap.add_argument("--row-weight", type=float, default=None,
+                    help="shard balance: cost = nnz + row_weight * rows (0 = nnz balance; default: the "
+                         "library's SHARD_ROW_WEIGHT)")
     ap.add_argument("--shard-balance", default="",
                     help="e.g. 2,4,8: time every shard of each N-way row partition one after another on this "
                          "GPU (the path has no collective, so the slowest shard predicts the N-GPU step) and "
                          "print that instead of the bench line")
-    ap.add_argument("--row-weights", default="0,5.4,10", help="row weights tried by --shard-balance")
+    ap.add_argument("--row-weights", default="0,3,5.4,8", help="row weights tried by --shard-balance")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.row_weight is None:
+        import vcsr_mc_b200 as vm
+        args.row_weight = vm.SHARD_ROW_WEIGHT
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -360,7 +391,10 @@ def main() -> None:
         # The reference's own CPU implementation of the path (oracle/_ref), rank 0 only.
         if rank != 0:
             return
-        config["plan"] = config["plan"].format(band_cols="kBandK")
+        config["path"] = ("the reference's fp64 CSR SpMM loop (src/main.cpp:202-207, built from its sources into "
+                          "oracle/_ref), fp64 accumulate, on host cores; B holds the GPU run's values" +
+                          (" rounded to fp16" if fp16 else ""))
+        config["plan"] = "reference CPU loop, rows split into one slice per host thread"
         try:
             M, N, rp, col, val = load_or_generate_csr(spec, 0, 1, lambda: None)
             cb = time_reference_cpu(M, N, rp, col, val, args.steps, args.warmup, args.cpu_sample_nnz, fp16)
@@ -606,7 +640,11 @@ def main() -> None:
                         "frac": both_ms / max(float(e2e_ms), 1e-6),
                         "how": "this step's H2D and D2H copies timed alone and at once, max over ranks"},
                "b_staging": ("each rank uploads 1/N of B, NCCL all-gather over NVLink" if world > 1 else
-                             "B uploaded whole")}
+                             "B uploaded whole"),
+               "a_resident": True,
+               "a_scope": "A's format is built and uploaded once before the timed region (persistent A, as the "
+                          "reference's upload_vcsr_mc_device); only B up, the SpMM and C down are timed per step",
+               "format_build": args.build, "format_build_upload_s": build_s}
         del Bd, Cd, hB, hC
 
     # Optional gather of C to rank 0 over NVLink (NCCL point-to-point), timed on its own: the
@@ -650,7 +688,7 @@ def main() -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cb = time_reference_cpu(M, N, rp, col, val, 3, 1, args.cpu_sample_nnz, fp16)
+            cb = time_reference_cpu(M, N, rp, col, val, args.steps, args.warmup, args.cpu_sample_nnz, fp16)
             cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model", "single_core")}
         except Exception as e:  # noqa: BLE001
             cpu = {"value": None, "unavailable": f"{type(e).__name__}: {e}"}

@@ -167,9 +167,16 @@ int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const vcsrmc_upload_o
 int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const int32_t* row_ptr, const int32_t* col,
                         const float* val, int fp32, int segw, int device,
                         const vcsrmc_upload_options* opts, void* stream, vcsrmc_device_format** out);
-/* half_scale (src/vcsr_mc.cu:14-22) of nnz fp32 values in device memory (current device),
- * blocking. Allocates nothing: its scratch word is a file-scope device array, and concurrent
- * calls in one process are serialised. */
+/* The fp16 range scale of nnz fp32 values that are already in device memory (current device):
+ * the largest |value| is reduced on the GPU and turned into the scale that vcsrmc_half_scale
+ * gives for the same values (1 when the largest magnitude is already in fp16's comfortable range).
+ * Blocking. Has no counterpart in the reference: it exists for callers that cannot allocate
+ * device memory (a caller running under a fixed memory budget or its own pool allocator, or a
+ * process whose allocator is not to be touched), so it makes no cudaMalloc, cudaFree or
+ * library allocation. Its scratch is one 32-bit word in a file-scope device array that every
+ * device loading this library holds until the process exits; the word is cleared on the stream
+ * before each reduction, and calls in one process are serialised by a lock, because two
+ * reductions overlapping on the GPU would race on that word. */
 int vcsrmc_half_scale_device(const float* val, int64_t nnz, void* stream, float* scale);
 /* Copies the SEGMENT arrays of a device format back into a host format (values as the device
  * holds them: FP16 formats keep them rounded to fp16). */

@@ -1,6 +1,7 @@
 """Multi-GPU host logic on CPU: world_size-2 `gloo` ranks, no GPU.
 
-Each rank takes its nnz-balanced block of rows (vcsrmc_partition_rows), builds the VCSR-MC
+Each rank takes its block of rows, balanced on nnz plus SHARD_ROW_WEIGHT per row
+(vcsrmc_partition_rows_weighted, the partition `bench.py --gpus N` uses), builds the VCSR-MC
 format of that block on its own (the reference builder applied to a row slice), and computes its
 rows of C with the fp64 oracle from the format alone. The ranks exchange their results; rank 0
 checks that the blocks tile the matrix and that the assembled C equals the single-process
@@ -54,7 +55,8 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
         A = vm.CSR.generate(vm.GEN_ZIPF, 1 << 11, seed=7)  # same matrix on every rank (seeded)
         rp, col, val = A.arrays()
         B = vm.gen_dense_host(A.N, 8, seed=7)
-        cuts = vm.partition_rows(rp, world)
+        w = vm.SHARD_ROW_WEIGHT  # the partition the benchmark's GPU ranks use
+        cuts = vm.partition_rows(rp, world, row_weight=w)
         r0, r1 = int(cuts[rank]), int(cuts[rank + 1])
         shard = A.row_slice(r0, r1)
         fmt = vm.csr_to_vcsr_mc(shard, fp32=True, segw=32).arrays()
@@ -77,9 +79,11 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
             ref = ob.spmm_fp64(rp, col, val, B)
             assert C.shape == ref.shape
             assert np.allclose(C, ref, rtol=1e-12, atol=1e-12)
-            # balance: each block holds about nnz/world entries (a row is never split)
-            nnz_blocks = [int(rp[cuts[k + 1]] - rp[cuts[k]]) for k in range(world)]
-            assert max(nnz_blocks) - min(nnz_blocks) <= int(np.max(np.diff(rp))) + 1
+            # balance: each block costs about (nnz + w * rows) / world; a row is never split, so blocks
+            # differ by at most one row's cost
+            cost = [float(rp[cuts[k + 1]] - rp[cuts[k]]) + w * float(cuts[k + 1] - cuts[k]) for k in range(world)]
+            assert max(cost) - min(cost) <= float(np.max(np.diff(rp))) + w + 1
+            assert cuts[0] == 0 and cuts[-1] == A.M and np.all(np.diff(cuts) >= 0)
             open(os.path.join(out_dir, "ok"), "w").close()
         dist.barrier()
     finally:

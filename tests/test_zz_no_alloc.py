@@ -1,5 +1,8 @@
-"""vcsrmc_half_scale_device: half_scale (src/vcsr_mc.cu:14-22) of device-resident values, computed
-without any device allocation (the reduction's scratch word is a file-scope device array)."""
+"""vcsrmc_half_scale_device: the fp16 range scale of values already in device memory, for callers
+that cannot allocate device memory (a fixed memory budget, their own pool allocator). The call makes
+no allocation: its reduction's scratch word is a file-scope device array, cleared before every call.
+Its result is checked against the oracle's scale of the same values, and device free memory must not
+change over repeated calls."""
 import ctypes
 
 import numpy as np

@@ -332,6 +332,12 @@ def gen_dense_device(out, seed: int, stream=None):
     return out
 
 
+# Row weight of the multi-GPU partition that the benchmark and the sharded path use: a block's
+# cost is nnz + SHARD_ROW_WEIGHT * rows, from a fit of measured per-shard times of the ROWS plan on
+# the 2^24-row R-MAT (a per-entry cost plus a per-row cost, the C row store and the row bookkeeping).
+SHARD_ROW_WEIGHT = 5.4
+
+
 def partition_rows(row_ptr: np.ndarray, parts: int, row_weight: float = 0.0) -> np.ndarray:
     """parts+1 row cuts balancing nnz + row_weight * rows per block (0: pure nnz balance)."""
     rp = np.ascontiguousarray(row_ptr, dtype=np.int32)

@@ -73,8 +73,22 @@ T read_one(const T* d, cudaStream_t st) {
     return h;
 }
 
+// SMs of the calling thread's current device (the builder's kernels run there).
+int current_sm_count() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+        cudaGetLastError();
+        return 1;
+    }
+    return sms;
+}
+
+// Grid-stride launches: enough blocks to fill every SM 64 times over (8 resident 256-thread
+// blocks per SM, eight waves), fewer for small inputs.
 unsigned blocks_for(int64_t n, int threads = 256) {
-    return unsigned(std::max<int64_t>(1, std::min<int64_t>((n + threads - 1) / threads, 148LL * 64)));
+    const int64_t cap = int64_t(current_sm_count()) * 64;
+    return unsigned(std::max<int64_t>(1, std::min<int64_t>((n + threads - 1) / threads, cap)));
 }
 
 // Row of entry p: the last r with row_ptr[r] <= p.

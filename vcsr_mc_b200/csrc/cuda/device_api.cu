@@ -279,9 +279,10 @@ namespace dev {
 cudaError_t gen_dense_device(int64_t rows, int cols, uint64_t seed, int f16, void* out, int64_t ld, cudaStream_t st) {
     const int64_t total = rows * int64_t(cols);
     if (total == 0) return cudaSuccess;
-    int sms = 148, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int sms = 0, dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, int64_t(sms) * 16);
     gen_dense_kernel<<<unsigned(blocks), 256, 0, st>>>(rows, cols, vrng_key(seed, VRNG_STREAM_DENSE), f16, out, ld);
     return cudaGetLastError();

@@ -108,6 +108,111 @@ std::vector<double> cpu_reference(const CSR& csr, const std::vector<float>& hB, 
     return ref;
 }
 
+// ---- checking, statistics and output --------------------------------------------------------
+// The interface kept from the reference's driver (src/main.cpp:257-304): the CSV columns and their
+// order, the acceptance bounds and the error messages. The code below is this driver's own.
+
+// Norms of a kernel's C against the fp64 CPU result, summed per thread block of rows.
+struct Fp64Comparison {
+    bool finite = true;  // every element of C is finite
+    double err_norm = 0, ref_norm = 0;
+    double rel_l2() const {
+        if (!finite) return INFINITY;
+        return ref_norm > 0 ? err_norm / ref_norm : err_norm;
+    }
+};
+
+Fp64Comparison compare_with_fp64(const std::vector<float>& got, const std::vector<double>& ref) {
+    Fp64Comparison c;
+    c.finite = std::all_of(got.begin(), got.end(), [](float x) { return std::isfinite(x); });
+    if (!c.finite) return c;
+    const int T = int(std::max(1u, std::min(16u, std::thread::hardware_concurrency())));
+    std::vector<double> e2(T, 0.0), r2(T, 0.0);
+    std::vector<std::thread> th;
+    for (int t = 0; t < T; ++t)
+        th.emplace_back([&, t] {
+            const size_t lo = got.size() * size_t(t) / size_t(T), hi = got.size() * size_t(t + 1) / size_t(T);
+            for (size_t i = lo; i < hi; ++i) {
+                const double d = double(got[i]) - ref[i];
+                e2[t] += d * d;
+                r2[t] += ref[i] * ref[i];
+            }
+        });
+    for (auto& x : th) x.join();
+    c.err_norm = std::sqrt(std::accumulate(e2.begin(), e2.end(), 0.0));
+    c.ref_norm = std::sqrt(std::accumulate(r2.begin(), r2.end(), 0.0));
+    return c;
+}
+
+// Acceptance of a result: ||C - ref|| <= norm_factor * ||ref|| + 1e-5 * sqrt(numel), and the
+// relative error at most rel_cap (the second bound keeps an all-zero C from passing on a reference
+// whose norm is tiny). FP16-input kernels get the looser pair.
+struct Acceptance {
+    double norm_factor, rel_cap;
+};
+Acceptance acceptance_for(const std::string& kernel) {
+    const bool fp16_inputs = kernel == "vcsr_mc" || kernel == "cusparse_fp16";
+    return fp16_inputs ? Acceptance{3e-3, 1e-1} : Acceptance{1e-4, 1e-2};
+}
+bool accepted(const Fp64Comparison& c, const Acceptance& a, size_t numel) {
+    if (!c.finite) return false;
+    const double bound = a.norm_factor * c.ref_norm + 1e-5 * std::sqrt(double(numel));
+    return c.err_norm <= bound && c.rel_l2() <= a.rel_cap;
+}
+
+// Mean and median of the timed launches.
+struct TimingSummary {
+    double mean = 0, median = 0;
+};
+TimingSummary summarize(std::vector<double> ms) {
+    TimingSummary s;
+    if (ms.empty()) return s;
+    s.mean = std::accumulate(ms.begin(), ms.end(), 0.0) / double(ms.size());
+    const size_t n = ms.size(), hi = n / 2;
+    std::nth_element(ms.begin(), ms.begin() + hi, ms.end());
+    s.median = ms[hi];
+    if (n % 2 == 0) s.median = 0.5 * (s.median + *std::max_element(ms.begin(), ms.begin() + hi));
+    return s;
+}
+
+// One line of output per kernel.
+struct ResultRow {
+    std::string algo, validation, plan;
+    double ms = 0, gflops = 0, rel_l2 = 0, ms_mean = 0, ms_median = 0;
+    double setup_ms = 0, convert_ms = 0, upload_ms = 0;
+};
+// Fixed columns of every row of a run.
+struct RunColumns {
+    std::string gpu, source;
+    int sm = 0, O = 0, segw = 0, bundle = 0, tileK = 0, repeat = 0;
+};
+constexpr const char* kCsvHeader =
+    "gpu,sm,mtx,O,segw,bundle,tileK,repeat,algo,ms,gflops,validation,rel_l2,setup_ms,ms_mean,ms_median,"
+    "convert_ms,upload_ms,plan";
+
+void print_result(const ResultRow& r, const RunColumns& run, bool csv) {
+    if (csv) {
+        std::printf("%s,%d,%s,%d,%d,%d,%d,%d,%s,%.9g,%.9g,%s,%.9g,%.6g,%.9g,%.9g,%.6g,%.6g,%s\n",
+                    csv_quote(run.gpu).c_str(), run.sm, csv_quote(run.source).c_str(), run.O, run.segw, run.bundle,
+                    run.tileK, run.repeat, r.algo.c_str(), r.ms, r.gflops, r.validation.c_str(), r.rel_l2,
+                    r.setup_ms, r.ms_mean, r.ms_median, r.convert_ms, r.upload_ms, r.plan.c_str());
+    } else {
+        std::printf("%-20s %10.6f %12.2f   %s (rel_l2=%.3g, setup %.3f ms, plan %s)\n", r.algo.c_str(), r.ms,
+                    r.gflops, r.validation.c_str(), r.rel_l2, r.setup_ms, r.plan.c_str());
+    }
+    std::fflush(stdout);
+}
+
+// Host wall time of one call, in milliseconds.
+template <class F>
+float host_ms(F&& f) {
+    using clock = std::chrono::steady_clock;
+    const clock::time_point start = clock::now();
+    f();
+    const std::chrono::duration<double, std::milli> spent = clock::now() - start;
+    return float(spent.count());
+}
+
 }  // namespace
 
 static int benchmark_main(int argc, char** argv) {
@@ -217,84 +322,71 @@ static int benchmark_main(int argc, char** argv) {
 
     std::vector<double> reference;
     if (check == "cpu") reference = cpu_reference(csr, hB, O);
-    if (csv)
-        std::printf("gpu,sm,mtx,O,segw,bundle,tileK,repeat,algo,ms,gflops,validation,rel_l2,setup_ms,ms_mean,ms_median,"
-                    "convert_ms,upload_ms,plan\n");
-    else
+    RunColumns run_cols;
+    run_cols.gpu = device.name;
+    run_cols.sm = device.major * 10 + device.minor;
+    run_cols.source = source;
+    run_cols.O = O;
+    run_cols.segw = segw;
+    run_cols.bundle = bundle;
+    run_cols.tileK = tileK;
+    run_cols.repeat = repeat;
+    if (csv) {
+        std::printf("%s\n", kCsvHeader);
+    } else {
         std::printf("Matrix: %d x %d, nnz=%d; O=%d segw=%d bundle=%d tileK=%d repeat=%d warmup=%d reorder=%s; "
-                    "reference=%s\nKernel                Time (ms)      GFLOP/s   Validation\n",
+                    "reference=%s\n",
                     csr.M, csr.N, csr.nnz, O, segw, bundle, tileK, repeat, warmup, reorder.c_str(), check.c_str());
-    auto wall_ms = [](auto&& f) {
-        const auto t0 = std::chrono::steady_clock::now();
-        f();
-        return std::chrono::duration<float, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        std::printf("Kernel                Time (ms)      GFLOP/s   Validation\n");
+    }
+    // One launch on a zeroed C (C += A*B), its event time in ms.
+    auto launch_once = [&](const std::function<float()>& run) {
+        cuda_ok(cudaMemsetAsync(dC, 0, elementsC * sizeof(float), st), "cudaMemsetAsync");
+        cuda_ok(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        const float ms = csr.nnz ? run() : 0.f;
+        cuda_ok(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        if (!std::isfinite(ms) || ms < 0) throw std::runtime_error("Invalid kernel timing");
+        return double(ms);
     };
+    // Warm-up launches (discarded), `repeat` timed launches, then the last C against the fp64 result.
     auto measure = [&](const char* name, const std::function<float()>& run, float setup_ms, float convert_ms,
                        float upload_ms, const char* plan_used) {
-        auto iterate = [&]() {
-            cuda_ok(cudaMemsetAsync(dC, 0, elementsC * sizeof(float), st), "cudaMemsetAsync");
-            cuda_ok(cudaStreamSynchronize(st), "cudaStreamSynchronize");
-            const float ms = csr.nnz ? run() : 0.f;
-            cuda_ok(cudaStreamSynchronize(st), "cudaStreamSynchronize");
-            if (!std::isfinite(ms) || ms < 0) throw std::runtime_error("Invalid kernel timing");
-            return double(ms);
-        };
-        for (int it = 0; it < warmup; ++it) iterate();
-        std::vector<double> times(repeat);
-        for (double& t : times) t = iterate();
-        double rel_l2 = 0;
-        bool failed = false;
+        for (int it = 0; it < warmup; ++it) launch_once(run);
+        std::vector<double> times;
+        times.reserve(size_t(repeat));
+        for (int it = 0; it < repeat; ++it) times.push_back(launch_once(run));
+        ResultRow row;
+        row.algo = name;
+        row.plan = plan_used;
+        row.validation = "unchecked";
         if (check != "none") {
             std::vector<float> result(elementsC);
             cuda_ok(cudaMemcpy(result.data(), dC, elementsC * sizeof(float), cudaMemcpyDeviceToHost), "cudaMemcpy");
-            double e2 = 0, r2 = 0;
-            bool nonfinite = false;
-            for (size_t i = 0; i < result.size(); ++i) {
-                if (!std::isfinite(result[i])) {
-                    if (!lenient) throw std::runtime_error(std::string(name) + ": non-finite output");
-                    nonfinite = true;
-                    break;
-                }
-                const double e = double(result[i]) - reference[i];
-                e2 += e * e;
-                r2 += reference[i] * reference[i];
-            }
-            const double err = std::sqrt(e2), norm = std::sqrt(r2);
-            rel_l2 = norm > 0 ? err / norm : err;
-            if (nonfinite) { rel_l2 = INFINITY; failed = true; }
-            const std::string kname(name);
-            const bool half = kname == "vcsr_mc" || kname == "cusparse_fp16";
-            const double tolerance = (half ? 3e-3 : 1e-4) * norm + 1e-5 * std::sqrt(double(elementsC));
-            if (!nonfinite && (err > tolerance || rel_l2 > (half ? 1e-1 : 1e-2))) {
-                if (!lenient)
-                    throw std::runtime_error(std::string(name) + ": correctness check failed, rel_l2=" +
-                                             std::to_string(rel_l2));
-                failed = true;
-            }
+            const Fp64Comparison cmp = compare_with_fp64(result, reference);
+            if (!cmp.finite && !lenient) throw std::runtime_error(std::string(name) + ": non-finite output");
+            row.rel_l2 = cmp.rel_l2();
+            const bool ok = accepted(cmp, acceptance_for(name), elementsC);
+            if (!ok && cmp.finite && !lenient)
+                throw std::runtime_error(std::string(name) + ": correctness check failed, rel_l2=" +
+                                         std::to_string(row.rel_l2));
+            row.validation = ok ? "pass" : "FAIL";
         }
-        const double ms_mean = std::accumulate(times.begin(), times.end(), 0.0) / repeat;
-        std::sort(times.begin(), times.end());
-        const double ms_median =
-            repeat % 2 ? times[repeat / 2] : 0.5 * (times[repeat / 2 - 1] + times[repeat / 2]);
-        const double ms = stat == "median" ? ms_median : ms_mean;
-        const double gflops = ms > 0 ? (2.0 * csr.nnz * O) / (ms * 1e6) : 0;
-        const char* validation = check == "none" ? "unchecked" : failed ? "FAIL" : "pass";
-        if (csv)
-            std::printf("%s,%d,%s,%d,%d,%d,%d,%d,%s,%.9g,%.9g,%s,%.9g,%.6g,%.9g,%.9g,%.6g,%.6g,%s\n",
-                        csv_quote(device.name).c_str(), device.major * 10 + device.minor, csv_quote(source).c_str(), O,
-                        segw, bundle, tileK, repeat, name, ms, gflops, validation, rel_l2, setup_ms, ms_mean, ms_median,
-                        convert_ms, upload_ms, plan_used);
-        else
-            std::printf("%-20s %10.6f %12.2f   %s (rel_l2=%.3g, setup %.3f ms, plan %s)\n", name, ms, gflops, validation,
-                        rel_l2, setup_ms, plan_used);
-        std::fflush(stdout);
+        const TimingSummary t = summarize(times);
+        row.ms_mean = t.mean;
+        row.ms_median = t.median;
+        row.ms = stat == "median" ? t.median : t.mean;
+        row.gflops = row.ms > 0 ? (2.0 * csr.nnz * O) / (row.ms * 1e6) : 0;
+        row.setup_ms = setup_ms;
+        row.convert_ms = convert_ms;
+        row.upload_ms = upload_ms;
+        print_result(row, run_cols, csv);
     };
 
     for (const bool fp32 : {false, true}) {
         const char* name = fp32 ? "vcsr_mc_fp32" : "vcsr_mc";
         if (!selected(name)) continue;
         VCSRMC V;
-        const float convert = wall_ms([&] { V = csr_to_vcsr_mc(csr, fp32, segw); });
+        const float convert = host_ms([&] { V = csr_to_vcsr_mc(csr, fp32, segw); });
         const bool use_b16 = b16 && !fp32;
         if (use_b16 && !dB16) {
             std::vector<__half> h(elementsB);
@@ -304,7 +396,7 @@ static int benchmark_main(int argc, char** argv) {
         }
         if (plan_id == VCSRMC_PLAN_AUTO && !use_b16) {
             // the reference's own call sequence (src/main.cpp:356-361)
-            const float upload = wall_ms([&] { upload_vcsr_mc_device(V); });
+            const float upload = host_ms([&] { upload_vcsr_mc_device(V); });
             measure(name, [&] { float ms = 0; run_vcsr_mc_spmm_gpu(V, dB, O, tileK, dC, st, ms); return ms; },
                     convert + upload, convert, upload, "auto");
             destroy_vcsr_mc_device(st);
@@ -318,7 +410,7 @@ static int benchmark_main(int argc, char** argv) {
             const int my_plan = (plan_id == VCSRMC_PLAN_BAND && fp32) ? VCSRMC_PLAN_ROWS : plan_id;
             const int mask = my_plan == VCSRMC_PLAN_BAND ? (1 << VCSRMC_PLAN_BAND) : 0;
             const char* my_plan_name = my_plan == plan_id ? plan.c_str() : "rows";
-            const float upload = wall_ms([&] { abi_ok(vcsrmc_upload_ex(hf, device_id, mask, st, &hd)); });
+            const float upload = host_ms([&] { abi_ok(vcsrmc_upload_ex(hf, device_id, mask, st, &hd)); });
             measure(name,
                     [&] {
                         cudaEvent_t a, b;
