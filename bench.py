@@ -355,6 +355,13 @@ def main() -> None:
                          "to the reference builder, about 15 s on config 4 and all host cores per rank)")
     ap.add_argument("--unit-nnz", type=int, default=0,
                     help="ROWS plan: entries per work unit (0 = the library's choice for the matrix)")
+    ap.add_argument("--hot-rows", type=int, default=0,
+                    help="ROWS plan hot columns (opt-in): rank this many most used columns (0 = none)")
+    ap.add_argument("--hot-budget-mib", type=int, default=0,
+                    help="hot columns: MiB of their B rows copied into a compact buffer per call (0 = no copy)")
+    ap.add_argument("--hot-persist", type=int, default=0, help="hot columns: persisting L2 window on the copy")
+    ap.add_argument("--hot-evict-first", type=int, default=0,
+                    help="hot columns: read the rows of unranked columns with evict-first loads")
     ap.add_argument("--row-weight", type=float, default=None,
                     help="shard balance: cost = nnz + row_weight * rows (0 = nnz balance; default: the "
                          "library's SHARD_ROW_WEIGHT)")
@@ -435,6 +442,8 @@ def main() -> None:
                                np.asarray(col[p0:p1]), np.asarray(val[p0:p1]))
     nthreads = max(1, cores // world)
     plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND}[args.plan]
+    hot = {"hot_rows": args.hot_rows, "hot_budget_mib": args.hot_budget_mib, "hot_persist": args.hot_persist,
+           "hot_evict_first": args.hot_evict_first}
     torch.cuda.synchronize()
     tb = time.time()
     if args.build == "device":
@@ -443,11 +452,11 @@ def main() -> None:
         d_col = torch.from_numpy(np.asarray(shard.arrays(copy=False)[1])).cuda()
         d_val = torch.from_numpy(np.asarray(shard.arrays(copy=False)[2])).cuda()
         dV = vm.build_vcsr_mc_device(d_rp, d_col, d_val, shard.M, shard.N, fp32=not fp16, segw=args.segw,
-                                     device=local, plans=[plan], rows_unit_nnz=args.unit_nnz)
+                                     device=local, plans=[plan], rows_unit_nnz=args.unit_nnz, **hot)
         del d_rp, d_col, d_val
     else:
         V = vm.csr_to_vcsr_mc(shard, fp32=not fp16, segw=args.segw, nthreads=nthreads)
-        dV = vm.upload_vcsr_mc_device(V, device=local, plans=[plan], rows_unit_nnz=args.unit_nnz)
+        dV = vm.upload_vcsr_mc_device(V, device=local, plans=[plan], rows_unit_nnz=args.unit_nnz, **hot)
         del V
     torch.cuda.synchronize()
     build_s = time.time() - tb
@@ -456,7 +465,8 @@ def main() -> None:
     info = dV.info()
     # this library's kernels per step: the SpMM kernel, plus (ROWS plan) the zeroing of the rows
     # split into chunks that are reduced into C
-    launches_per_step = 1 + (1 if plan == vm.PLAN_ROWS and info["n_split_rows"] > 0 else 0)
+    launches_per_step = 1 + (1 if plan == vm.PLAN_ROWS and info["n_split_rows"] > 0 else 0) + \
+        (1 if plan == vm.PLAN_ROWS and info["n_hot"] > 0 and args.hot_budget_mib > 0 else 0)
     groups, slots, items = info["n_groups"], info["n_slots"], info["n_items"]
     config["plan"] = config["plan"].format(band_cols=info["band_cols"])
     log(f"rank {rank}: rows [{r0},{r1}) nnz {p1 - p0} format build + upload ({args.build}) {build_s:.2f}s "
@@ -715,7 +725,8 @@ def main() -> None:
                        "groups": groups, "slots": slots, "items": items, "device_status": status,
                        "format_build": args.build, "format_build_upload_s": build_s,
                        "rows_unit_nnz": info["rows_unit_nnz"], "band_rows": info["band_rows"],
-                       "band_tiles": info["n_tiles"], "clock_samples": clk["samples"]},
+                       "band_tiles": info["n_tiles"], "clock_samples": clk["samples"],
+                       "hot_columns": {**hot, "n_hot": info["n_hot"]}},
         }
         emit(line)
     dV.free()

@@ -152,7 +152,19 @@ typedef struct {
                               rows with more entries are split into chunks of this size.
                               0 = chosen from the matrix so that every SM gets enough units.  */
     int32_t band_rows;     /* BAND plan: rows per band, 1 .. 128; 0 = chosen from the matrix    */
-    int32_t reserved[5];   /* must be 0                                                        */
+    /* ROWS plan, hot columns (off by default). The most used columns of A get a rank (most
+     * entries first); a call can then copy their rows of B into one compact buffer that the
+     * next gathers read, optionally under a persisting L2 window, and read the other rows with
+     * evict-first loads. C is the same either way. On the 2^24-row R-MAT none of these made
+     * the SpMM faster on a B200 (the kernel is bound by gathers in flight, not DRAM bytes); they
+     * are kept for matrices and GPUs where L2 policy decides.                                  */
+    int32_t hot_rows;       /* 0 = no hot columns; > 0 = rank at most this many columns       */
+    int32_t hot_budget_mib; /* MiB of hot B rows copied per call, 0 = no copy (0 .. 4096)      */
+    int32_t hot_persist;    /* 1 = the copied rows get a persisting L2 access-policy window;
+                               raises this process's persisting-L2 limit on the device up to
+                               the device's maximum (a context setting, gone at exit)         */
+    int32_t hot_evict_first;/* 1 = rows of unranked columns are read with evict-first loads  */
+    int32_t reserved[1];    /* must be 0                                                       */
 } vcsrmc_upload_options;
 int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const vcsrmc_upload_options* opts,
                        void* stream, vcsrmc_device_format** out);
@@ -192,12 +204,21 @@ typedef struct {
     int32_t rows_unit_nnz, n_split_rows;  /* ROWS: entries per unit, rows split into chunks */
     int32_t band_rows, n_bands;           /* BAND layout                                    */
     int64_t n_tiles;
-    int32_t band_cols, reserved;          /* BAND: columns per tile (this build's tile width) */
+    int32_t band_cols;                    /* BAND: columns per tile (this build's tile width) */
+    int32_t n_hot;                        /* ROWS: ranked hot columns (0: none)              */
 } vcsrmc_device_info;
 int vcsrmc_device_info_get(const vcsrmc_device_format* d, vcsrmc_device_info* out);
 /* Error flags raised by kernels of this format since the last clear (bit 0: a bounded wait
  * timed out). Blocking read. */
 int vcsrmc_device_status(const vcsrmc_device_format* d, uint32_t* flags, int clear);
+
+/* Diagnostic of the bounded device waits (no counterpart in the reference): one CTA on d's device
+ * holds tensor memory and waits up to budget_cycles SM clock cycles (1 .. 2e9) on an mbarrier
+ * phase that cannot complete, as an SpMM kernel would on a lost copy. The wait must expire: it
+ * sets the timeout flag in d's status word (vcsrmc_device_status), frees the tensor memory, and
+ * *completed = 0 (1 would mean the phase completed). Blocking; nothing else is in flight. */
+int vcsrmc_device_wait_check(const vcsrmc_device_format* d, int64_t budget_cycles, void* stream,
+                             int* completed);
 
 /* ---- SpMM: src/vcsr_mc.cu:352-394 run_vcsr_mc_spmm_gpu ----------------------------------
  * C[M x O] (+)= A * B[N x O]. B is fp32 (both formats) or fp16 (FP16 format only), with row

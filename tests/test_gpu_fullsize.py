@@ -8,7 +8,9 @@ not depend on size:
     1e-4 of |A| (|B| |x|) (fp32 accumulation error; the reference side uses the A values the GPU
     multiplies, i.e. rounded to fp16 on the FP16 path).
 
-Config 4 (R-MAT 2^24, 263 M nnz) builds its format on the GPU (vcsrmc_build_device).
+Config 4 (R-MAT 2^24, 263 M nnz) runs on a GPU-built format (vcsrmc_build_device; FP16 and FP32,
+every plan) and on a host-built one (the builder that is bit-identical to the reference's), and
+config 5's wide widths (O = 256, 512) run on the config-2 matrix with and without RCM.
 """
 import numpy as np
 import pytest
@@ -73,25 +75,37 @@ def check_checksums(torch, rp, col, val, B, C, fp32, scale, seed):
         assert np.all(np.isfinite(y)) and worst <= 0.0, f"checksum exceeds its bound by {worst:.3e}"
 
 
-CASES = [("c1", False, vm.PLAN_AUTO), ("c1", True, vm.PLAN_AUTO), ("c2", False, vm.PLAN_AUTO),
-         ("c2", True, vm.PLAN_AUTO), ("c3", False, vm.PLAN_AUTO), ("c3", False, vm.PLAN_ROWS),
-         ("c3", False, vm.PLAN_SEGMENT), ("c3", True, vm.PLAN_AUTO), ("c4", False, vm.PLAN_AUTO)]
+# (config, FP32 format, plan, where the format is built, hot-column upload options)
+HOT = {"hot_rows": 393216, "hot_budget_mib": 96}
+CASES = [("c1", False, vm.PLAN_AUTO, "host", None), ("c1", True, vm.PLAN_AUTO, "host", None),
+         ("c2", False, vm.PLAN_AUTO, "host", None), ("c2", True, vm.PLAN_AUTO, "host", None),
+         ("c3", False, vm.PLAN_AUTO, "host", None), ("c3", False, vm.PLAN_ROWS, "host", None),
+         ("c3", False, vm.PLAN_SEGMENT, "host", None), ("c3", True, vm.PLAN_AUTO, "host", None),
+         ("c4", False, vm.PLAN_AUTO, "device", None), ("c4", False, vm.PLAN_ROWS, "device", None),
+         ("c4", False, vm.PLAN_SEGMENT, "device", None), ("c4", True, vm.PLAN_AUTO, "device", None),
+         ("c4", True, vm.PLAN_ROWS, "device", None), ("c4", True, vm.PLAN_SEGMENT, "device", None),
+         ("c4", False, vm.PLAN_ROWS, "host", None), ("c4", False, vm.PLAN_ROWS, "device", HOT)]
+PLAN_NAMES = {0: "auto", 1: "segment", 2: "rows", 3: "band"}
 
 
-@pytest.mark.parametrize("name,fp32,plan", CASES,
-                         ids=[f"{n}-{'fp32' if f else 'fp16'}-{ {0: 'auto', 1: 'segment', 2: 'rows'}[p]}"
-                              for n, f, p in CASES])
-def test_full_size(cuda, name, fp32, plan):
+@pytest.mark.parametrize("name,fp32,plan,build,hot", CASES,
+                         ids=[f"{n}-{'fp32' if f else 'fp16'}-{PLAN_NAMES[p]}-{b}{'-hot' if h else ''}"
+                              for n, f, p, b, h in CASES])
+def test_full_size(cuda, name, fp32, plan, build, hot):
+    """Configs 1-4 at full size; config 4 on a GPU-built format (FP16 and FP32, every plan), on a
+    host-built one (bit-identical to the reference builder), and with hot columns."""
     torch = cuda
     A = matrix(name)
     rp, col, val = A.arrays(copy=False)
-    if name == "c4":
+    if build == "device":
         t = lambda x: torch.from_numpy(np.asarray(x)).cuda()
-        dV = vm.build_vcsr_mc_device(t(rp), t(col), t(val), A.M, A.N, fp32=fp32, segw=32)
+        dV = vm.build_vcsr_mc_device(t(rp), t(col), t(val), A.M, A.N, fp32=fp32, segw=32, **(hot or {}))
     else:
-        dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=fp32, segw=32), device=0)
+        dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=fp32, segw=32), device=0, **(hot or {}))
     if name == "c3" and not fp32 and plan == vm.PLAN_AUTO:
         assert vm.PLAN_BAND in dV.info()["plans"]  # the default layouts add BAND on the stencil
+    if hot:
+        assert dV.info()["n_hot"] == hot["hot_rows"]
     B = torch.empty((A.N, 128), dtype=torch.float32 if fp32 else torch.float16, device="cuda")
     vm.gen_dense_device(B, seed=11)
     C = torch.full((A.M, 128), float("nan"), device="cuda")
@@ -103,3 +117,44 @@ def test_full_size(cuda, name, fp32, plan):
     dV.free()
     del B, C
     torch.cuda.empty_cache()
+
+
+# Config 5: the config-2 matrix at the sweep's wide dense widths, both segment widths, with and without
+# the reference's RCM column permutation (include/reorder.hpp), on the ROWS plan and on the SEGMENT
+# plan at tileK 128 and 256 (the format does not depend on tileK; tileK 256 is new, the reference
+# stops at 128).
+_c5 = {}
+
+
+def c5_problem(rcm: bool, O: int):
+    key = (rcm, O)
+    if key not in _c5:
+        _c5.clear()
+        A = vm.CSR.generate(vm.GEN_ZIPF, 262144, seed=0)
+        B = vm.gen_dense_host(A.N, O, seed=21)
+        if rcm:
+            B = vm.apply_column_permutation(A, B, vm.rcm_column_order(A))
+        _c5[key] = (A, B)
+    return _c5[key]
+
+
+C5 = [(O, fp32, segw, rcm, plan, tk) for O in (256, 512) for rcm in (False, True) for fp32 in (False, True)
+      for segw in (16, 32) for plan, tk in ((vm.PLAN_ROWS, 128), (vm.PLAN_SEGMENT, 128), (vm.PLAN_SEGMENT, 256))]
+
+
+@pytest.mark.parametrize("O,fp32,segw,rcm,plan,tileK", C5,
+                         ids=[f"O{o}-{'fp32' if f else 'fp16'}-s{w}-{'rcm' if r else 'natural'}-{PLAN_NAMES[p]}-tk{t}"
+                              for o, f, w, r, p, t in C5])
+def test_config5_wide(cuda, O, fp32, segw, rcm, plan, tileK):
+    torch = cuda
+    A, B32 = c5_problem(rcm, O)
+    rp, col, val = A.arrays(copy=False)
+    dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=fp32, segw=segw), device=0, plans=[plan])
+    B = torch.from_numpy(B32).to(device="cuda", dtype=torch.float32 if fp32 else torch.float16)
+    C = torch.full((A.M, O), float("nan"), device="cuda")
+    vm.spmm(dV, B, C, tileK=tileK, accumulate=False, plan=plan)
+    torch.cuda.synchronize()
+    assert dV.status() == 0
+    check_sampled_rows(torch, rp, col, val, B, C, sampled_rows(rp, A.M, np.random.default_rng(5)), fp32)
+    check_checksums(torch, rp, col, val, B, C, fp32, dV.scale, seed=6)
+    dV.free()

@@ -38,12 +38,13 @@ class DeviceInfo(ctypes.Structure):
                 ("n_groups", ctypes.c_int64), ("n_slots", ctypes.c_int64), ("n_items", ctypes.c_int64),
                 ("n_units", ctypes.c_int64), ("rows_unit_nnz", ctypes.c_int32), ("n_split_rows", ctypes.c_int32),
                 ("band_rows", ctypes.c_int32), ("n_bands", ctypes.c_int32),
-                ("n_tiles", ctypes.c_int64), ("band_cols", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("n_tiles", ctypes.c_int64), ("band_cols", ctypes.c_int32), ("n_hot", ctypes.c_int32)]
 
 
 class UploadOptions(ctypes.Structure):
     _fields_ = [("plans", ctypes.c_int32), ("rows_unit_nnz", ctypes.c_int32), ("band_rows", ctypes.c_int32),
-                ("reserved", ctypes.c_int32 * 5)]
+                ("hot_rows", ctypes.c_int32), ("hot_budget_mib", ctypes.c_int32), ("hot_persist", ctypes.c_int32),
+                ("hot_evict_first", ctypes.c_int32), ("reserved", ctypes.c_int32 * 1)]
 
 
 class CsrView(ctypes.Structure):
@@ -99,6 +100,7 @@ PROTOTYPES = {
                                    _pp]),
     "vcsrmc_device_download": (_int, [_p, _pp]),
     "vcsrmc_half_scale_device": (_int, [_p, _i64, _p, ctypes.POINTER(ctypes.c_float)]),
+    "vcsrmc_device_wait_check": (_int, [_p, _i64, _p, ctypes.POINTER(ctypes.c_int)]),
     "vcsrmc_device_info_get": (_int, [_p, ctypes.POINTER(DeviceInfo)]),
     "vcsrmc_device_free": (_int, [_p]),
     "vcsrmc_device_status": (_int, [_p, ctypes.POINTER(ctypes.c_uint32), _int]),

@@ -239,23 +239,37 @@ class DeviceVCSRMC:
         return f.value
 
 
-def upload_vcsr_mc_device(V: VCSRMC, device: int = 0, stream=None, plans=None,
-                          rows_unit_nnz: int = 0, band_rows: int = 0) -> DeviceVCSRMC:
-    """Copies the format to `device`. plans: iterable of PLAN_SEGMENT / PLAN_ROWS / PLAN_BAND
-    layouts to make resident (default: SEGMENT and ROWS, plus BAND for FP16 formats whose
-    column tiles are dense enough; BAND needs the FP16 format). rows_unit_nnz: entries per ROWS-plan work unit (0 = the library's
-    choice for this matrix). band_rows: rows per BAND-plan band, 1 .. 128 (0 = chosen)."""
+def _upload_options(plans, rows_unit_nnz: int, band_rows: int, hot_rows: int, hot_budget_mib: int,
+                    hot_persist: int, hot_evict_first: int) -> "_lib.UploadOptions":
     opts = _lib.UploadOptions()
     opts.plans = 0 if plans is None else sum(1 << p for p in set(plans))
     opts.rows_unit_nnz = rows_unit_nnz
     opts.band_rows = band_rows
+    opts.hot_rows = hot_rows
+    opts.hot_budget_mib = hot_budget_mib
+    opts.hot_persist = hot_persist
+    opts.hot_evict_first = hot_evict_first
+    return opts
+
+
+def upload_vcsr_mc_device(V: VCSRMC, device: int = 0, stream=None, plans=None,
+                          rows_unit_nnz: int = 0, band_rows: int = 0, hot_rows: int = 0, hot_budget_mib: int = 0,
+                          hot_persist: int = 0, hot_evict_first: int = 0) -> DeviceVCSRMC:
+    """Copies the format to `device`. plans: iterable of PLAN_SEGMENT / PLAN_ROWS / PLAN_BAND
+    layouts to make resident (default: SEGMENT and ROWS, plus BAND for FP16 formats whose
+    column tiles are dense enough; BAND needs the FP16 format). rows_unit_nnz: entries per ROWS-plan work unit (0 = the library's
+    choice for this matrix). band_rows: rows per BAND-plan band, 1 .. 128 (0 = chosen).
+    hot_rows / hot_budget_mib / hot_persist / hot_evict_first: the ROWS plan's hot columns, off by
+    default (vcsrmc_upload_options)."""
+    opts = _upload_options(plans, rows_unit_nnz, band_rows, hot_rows, hot_budget_mib, hot_persist, hot_evict_first)
     h = ctypes.c_void_p()
     call("vcsrmc_upload_opts", V.handle, device, ctypes.byref(opts), _stream_handle(stream), ctypes.byref(h))
     return DeviceVCSRMC(h, V, device)
 
 
 def build_vcsr_mc_device(row_ptr, col, val, M: int, N: int, fp32: bool = False, segw: int = 16, device: int = 0,
-                         stream=None, plans=None, rows_unit_nnz: int = 0, band_rows: int = 0) -> DeviceVCSRMC:
+                         stream=None, plans=None, rows_unit_nnz: int = 0, band_rows: int = 0, hot_rows: int = 0,
+                         hot_budget_mib: int = 0, hot_persist: int = 0, hot_evict_first: int = 0) -> DeviceVCSRMC:
     """Builds the format on the GPU from a CSR already in device memory (torch tensors: int32
     row_ptr[M+1], int32 col[nnz], float32 val[nnz], rows with strictly ascending columns) and
     keeps its plan layouts resident there. Equal-count rows of a segment come in ascending row
@@ -264,10 +278,7 @@ def build_vcsr_mc_device(row_ptr, col, val, M: int, N: int, fp32: bool = False, 
     for t, dt in ((row_ptr, torch.int32), (col, torch.int32), (val, torch.float32)):
         if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == dt and t.is_contiguous()):
             raise VcsrmcError(_lib.INVALID_ARG, "row_ptr/col/val must be contiguous CUDA tensors (int32, int32, float32)")
-    opts = _lib.UploadOptions()
-    opts.plans = 0 if plans is None else sum(1 << p for p in set(plans))
-    opts.rows_unit_nnz = rows_unit_nnz
-    opts.band_rows = band_rows
+    opts = _upload_options(plans, rows_unit_nnz, band_rows, hot_rows, hot_budget_mib, hot_persist, hot_evict_first)
     h = ctypes.c_void_p()
     call("vcsrmc_build_device", M, N, int(col.numel()), ctypes.c_void_p(row_ptr.data_ptr()),
          ctypes.c_void_p(col.data_ptr()), ctypes.c_void_p(val.data_ptr()), 1 if fp32 else 0, segw, device,

@@ -711,6 +711,80 @@ BandLayout build_band_layout(const int* row_ptr, const int* col, const float* va
     return L;
 }
 
+// ---- hot columns of the ROWS plan ------------------------------------------------------------
+namespace {
+
+__global__ void column_count_kernel(const int* __restrict__ cols, int64_t nnz, unsigned* __restrict__ count) {
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < nnz; i += int64_t(gridDim.x) * blockDim.x)
+        atomicAdd(count + cols[i], 1u);
+}
+
+// key = ~count, so that an ascending sort orders columns by descending count; counts the columns
+// used at all and those used at least twice.
+__global__ void column_key_kernel(const unsigned* __restrict__ count, int N, unsigned* __restrict__ key,
+                                  int* __restrict__ id, unsigned long long* __restrict__ used) {
+    for (int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; c < N; c += int64_t(gridDim.x) * blockDim.x) {
+        const unsigned n = count[c];
+        key[c] = ~n;
+        id[c] = int(c);
+        if (n >= 1) atomicAdd(used, 1ull);
+        if (n >= 2) atomicAdd(used + 1, 1ull);
+    }
+}
+
+// rank_of[col] = rank for the first k columns of the sorted order.
+__global__ void hot_rank_kernel(const int* __restrict__ sorted_id, int k, int* __restrict__ rank_of) {
+    for (int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; r < k; r += int64_t(gridDim.x) * blockDim.x)
+        rank_of[sorted_id[r]] = int(r);
+}
+
+__global__ void hot_rewrite_kernel(int* __restrict__ cols, int64_t nnz, const int* __restrict__ rank_of) {
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < nnz; i += int64_t(gridDim.x) * blockDim.x) {
+        const int r = rank_of[cols[i]];
+        if (r >= 0) cols[i] = ~r;
+    }
+}
+
+}  // namespace
+
+int* build_hot_columns(int* cols, int64_t nnz, int N, int max_hot, int* n_hot, cudaStream_t st) {
+    *n_hot = 0;
+    if (max_hot <= 0 || nnz <= 0 || N <= 0) return nullptr;
+    const size_t n = static_cast<size_t>(N);
+    Buf<unsigned> count(n), key(n), skey(n);
+    Buf<int> id(n), sid(n);
+    Buf<unsigned long long> tally(2);
+    check(cudaMemsetAsync(count.p, 0, sizeof(unsigned) * n, st), "cudaMemsetAsync");
+    check(cudaMemsetAsync(tally.p, 0, sizeof(unsigned long long) * 2, st), "cudaMemsetAsync");
+    column_count_kernel<<<blocks_for(nnz), 256, 0, st>>>(cols, nnz, count.p);
+    check(cudaGetLastError(), "column_count_kernel");
+    column_key_kernel<<<blocks_for(N), 256, 0, st>>>(count.p, N, key.p, id.p, tally.p);
+    check(cudaGetLastError(), "column_key_kernel");
+    {
+        size_t tmp = 0;
+        check(cub::DeviceRadixSort::SortPairs(nullptr, tmp, key.p, skey.p, id.p, sid.p, N, 0, 32, st), "cub sort");
+        Buf<uint8_t> t(tmp);
+        check(cub::DeviceRadixSort::SortPairs(t.p, tmp, key.p, skey.p, id.p, sid.p, N, 0, 32, st), "cub sort");
+    }
+    unsigned long long used[2] = {0, 0};
+    check(cudaMemcpyAsync(used, tally.p, sizeof used, cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync");
+    check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    const int k = int(std::min<unsigned long long>(used[1], (unsigned long long)max_hot));
+    if (k <= 0) return nullptr;
+    Buf<int> rank_of(n);
+    check(cudaMemsetAsync(rank_of.p, 0xff, sizeof(int) * n, st), "cudaMemsetAsync");
+    hot_rank_kernel<<<blocks_for(k), 256, 0, st>>>(sid.p, k, rank_of.p);
+    check(cudaGetLastError(), "hot_rank_kernel");
+    hot_rewrite_kernel<<<blocks_for(nnz), 256, 0, st>>>(cols, nnz, rank_of.p);
+    check(cudaGetLastError(), "hot_rewrite_kernel");
+    Buf<int> hot(static_cast<size_t>(k));
+    check(cudaMemcpyAsync(hot.p, sid.p, sizeof(int) * static_cast<size_t>(k), cudaMemcpyDeviceToDevice, st),
+          "cudaMemcpyAsync");
+    check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    *n_hot = k;
+    return hot.release();
+}
+
 bool device_validate(const SegmentLayout* seg, const RowsLayout* rows, int M, int N, int segw, cudaStream_t st) {
     Buf<int> bad(1);
     check(cudaMemsetAsync(bad.p, 0, sizeof(int), st), "cudaMemsetAsync");

@@ -12,8 +12,11 @@ namespace dev {
 
 constexpr uint32_t kStatusTimeout = 1u;  // a bounded wait expired
 
-// About one second at the B200's boost clock.
-constexpr long long kWaitBudgetCycles = 2000000000LL;
+// About one second at the B200's boost clock; a build may set another budget.
+#ifndef VCSRMC_WAIT_BUDGET_CYCLES
+#define VCSRMC_WAIT_BUDGET_CYCLES 2000000000LL
+#endif
+constexpr long long kWaitBudgetCycles = VCSRMC_WAIT_BUDGET_CYCLES;
 
 struct DeviceFormatView {
     const int2* items;     // {gbeg, gend}
@@ -57,13 +60,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Waits for the phase with the given parity to complete; false if the budget ran out.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// Waits for the phase with the given parity to complete; false if the budget (SM clock cycles) ran
+// out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  long long budget = kWaitBudgetCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (clock64() - t0 > kWaitBudgetCycles) return false;
+        if (clock64() - t0 > budget) return false;
     }
 }
 

@@ -30,6 +30,7 @@
 #include "plan_band.hpp"
 #include "plan_rows.hpp"
 #include "spmm_launch.hpp"
+#include "wait_check.hpp"
 
 struct vcsrmc_device_format {
     int device = 0;
@@ -61,6 +62,16 @@ struct vcsrmc_device_format {
     int* tile_col = nullptr;
     int* tile_eptr = nullptr;
     uint32_t* ents = nullptr;
+    // ROWS plan, hot columns (RowHotView): ranked columns, and the compact copy of their B rows
+    // that each call refreshes (grown on demand; launches of one handle are ordered).
+    int* hot_cols = nullptr;
+    int n_hot = 0;
+    int64_t hot_budget = 0;
+    bool hot_persist = false;
+    bool hot_evict_first = false;
+    void* hot_buf = nullptr;
+    int64_t hot_buf_bytes = 0;
+    std::mutex hot_mu;
 };
 
 namespace vcsrmc {
@@ -122,6 +133,14 @@ void free_device(vcsrmc_device_format* d) {
     cudaFree(d->tile_col);
     cudaFree(d->tile_eptr);
     cudaFree(d->ents);
+    cudaFree(d->hot_cols);
+    cudaFree(d->hot_buf);
+    // Lines marked persisting stay in L2's set-aside until reset and slow later kernels: return
+    // them to normal once the handle that marked them is gone.
+    if (d->hot_persist && d->n_hot > 0 && d->hot_budget > 0) {
+        cudaCtxResetPersistingL2Cache();
+        cudaGetLastError();
+    }
     if (prev >= 0) cudaSetDevice(prev);
     delete d;
 }
@@ -159,6 +178,57 @@ void validate_format(const VCSRMC& v) {
         for (int g = b + 1; g < e; ++g)
             if (v.group_seg_base[g] != v.group_seg_base[b]) bad("item spans segments");
     }
+}
+
+// ROWS plan hot columns (RowHotView): the most MiB of B rows one call may copy.
+constexpr int kHotBudgetMiBMax = 4096;
+
+void check_hot_options(const vcsrmc_upload_options& o) {
+    if (o.hot_rows < 0) throw StatusError(VCSRMC_INVALID_ARG, "hot_rows must be 0 or positive");
+    if (o.hot_budget_mib < 0 || o.hot_budget_mib > kHotBudgetMiBMax)
+        throw StatusError(VCSRMC_INVALID_ARG, "hot_budget_mib must be in [0, 4096]");
+    if (o.hot_persist < 0 || o.hot_persist > 1) throw StatusError(VCSRMC_INVALID_ARG, "hot_persist must be 0 or 1");
+    if (o.hot_evict_first < 0 || o.hot_evict_first > 1)
+        throw StatusError(VCSRMC_INVALID_ARG, "hot_evict_first must be 0 or 1");
+}
+
+// Ranks the hot columns of a resident ROWS layout (rewriting its device cols) as the options ask,
+// and, for a persisting window, raises this process's persisting-L2 limit on the device to the
+// copy budget (at most the device's maximum).
+void make_hot_columns(vcsrmc_device_format* d, int64_t nnz, const vcsrmc_upload_options& o, cudaStream_t st) {
+    d->hot_budget = int64_t(o.hot_budget_mib) << 20;
+    d->hot_persist = o.hot_persist == 1;
+    d->hot_evict_first = o.hot_evict_first == 1;
+    if (o.hot_rows <= 0 || !d->has_rows) return;
+    d->hot_cols = dev::build_hot_columns(d->cols, nnz, d->N, o.hot_rows, &d->n_hot, st);
+    if (d->n_hot > 0 && d->hot_persist && d->hot_budget > 0) {
+        int max_persist = 0;
+        size_t cur = 0;
+        cuda_check(cudaDeviceGetAttribute(&max_persist, cudaDevAttrMaxPersistingL2CacheSize, d->device),
+                   "cudaDeviceGetAttribute");
+        cuda_check(cudaDeviceGetLimit(&cur, cudaLimitPersistingL2CacheSize), "cudaDeviceGetLimit");
+        const size_t want = size_t(std::min<int64_t>(d->hot_budget, max_persist));
+        if (cur < want) cuda_check(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, want), "cudaDeviceSetLimit");
+    }
+}
+
+// The hot-row buffer for a call whose B rows are row_bytes apart: grown (after the stream's
+// earlier work, which may still read the old one) when the copy needs more than it holds.
+void ensure_hot_buffer(const vcsrmc_device_format* cd, int64_t row_bytes, cudaStream_t st) {
+    auto* d = const_cast<vcsrmc_device_format*>(cd);
+    if (d->n_hot <= 0 || row_bytes <= 0) return;
+    const int64_t need = std::min<int64_t>(d->hot_budget, int64_t(d->n_hot) * row_bytes);
+    if (need < row_bytes) return;
+    std::lock_guard<std::mutex> lock(d->hot_mu);
+    if (d->hot_buf_bytes >= need) return;
+    if (d->hot_buf) {
+        cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        cudaFree(d->hot_buf);
+        d->hot_buf = nullptr;
+        d->hot_buf_bytes = 0;
+    }
+    cuda_check(cudaMalloc(&d->hot_buf, size_t(need)), "cudaMalloc");
+    d->hot_buf_bytes = need;
 }
 
 dev::DeviceFormatView view_of(const vcsrmc_device_format* d) {
@@ -226,6 +296,15 @@ void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int6
         P.n_split_rows = d->n_split_rows;
         P.M = d->M;
         P.scale = d->scale;
+        const int64_t row_bytes = ldb * (b_dtype == VCSRMC_F16 ? 2 : 4);
+        ensure_hot_buffer(d, row_bytes, st);
+        P.hot.hot_cols = d->hot_cols;
+        P.hot.n_hot = d->n_hot;
+        P.hot.buf = d->hot_buf;
+        P.hot.buf_bytes = d->hot_buf_bytes;
+        P.hot.budget_bytes = d->hot_budget;
+        P.hot.persist = d->hot_persist;
+        P.hot.cold_hint = d->hot_evict_first;
         e = dev::spmm_rows(P, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, C, ldc, accumulate != 0, st);
         cuda_check(e, "SpMM launch (rows plan)");
         return;
@@ -311,6 +390,7 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
             throw StatusError(VCSRMC_INVALID_ARG, "rows_unit_nnz must be 0 or a power of two in [16, 1024]");
         if (opts->band_rows < 0 || opts->band_rows > dev::kBandRows)
             throw StatusError(VCSRMC_INVALID_ARG, "band_rows must be 0 or in [1, 128]");
+        check_hot_options(*opts);
         const VCSRMC& v = f->v;
         validate_format(v);
         if (device < 0) cuda_check(cudaGetDevice(&device), "cudaGetDevice");
@@ -405,6 +485,7 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
                 }
                 cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
                 d->has_rows = true;
+                make_hot_columns(d, int64_t(rv.cols.size()), *opts, st);
             }
             cuda_check(cudaMalloc(&d->status, sizeof(uint32_t)), "cudaMalloc");
             cuda_check(cudaMemsetAsync(d->status, 0, sizeof(uint32_t), st), "cudaMemsetAsync");
@@ -454,6 +535,7 @@ VCSRMC_EXPORT int vcsrmc_device_info_get(const vcsrmc_device_format* d, vcsrmc_d
         i.n_bands = d->n_bands;
         i.n_tiles = d->n_tiles;
         i.band_cols = dev::kBandK;
+        i.n_hot = d->n_hot;
         *out = i;
     });
 }
@@ -464,6 +546,27 @@ VCSRMC_EXPORT int vcsrmc_device_status(const vcsrmc_device_format* d, uint32_t* 
         DeviceGuard guard(d->device);
         cuda_check(cudaMemcpy(flags, d->status, sizeof(uint32_t), cudaMemcpyDeviceToHost), "cudaMemcpy");
         if (clear) cuda_check(cudaMemset(d->status, 0, sizeof(uint32_t)), "cudaMemset");
+    });
+}
+
+VCSRMC_EXPORT int vcsrmc_device_wait_check(const vcsrmc_device_format* d, int64_t budget_cycles, void* stream,
+                                           int* completed) {
+    return guarded([&] {
+        if (!d || !completed) throw StatusError(VCSRMC_INVALID_ARG, "NULL argument");
+        if (budget_cycles < 1 || budget_cycles > dev::kWaitBudgetCycles)
+            throw StatusError(VCSRMC_INVALID_ARG, "budget_cycles must be in [1, 2e9]");
+        DeviceGuard guard(d->device);
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        uint32_t* flag = nullptr;
+        cuda_check(cudaMalloc(&flag, sizeof(uint32_t)), "cudaMalloc");
+        uint32_t h = 0;
+        cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(uint32_t), st);
+        if (e == cudaSuccess) e = dev::bounded_wait_check(d->status, budget_cycles, flag, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(&h, flag, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        cudaFree(flag);
+        cuda_check(e, "bounded wait check");
+        *completed = int(h);
     });
 }
 
@@ -547,6 +650,7 @@ VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const i
             throw StatusError(VCSRMC_INVALID_ARG, "rows_unit_nnz must be 0 or a power of two in [16, 1024]");
         if (o.band_rows < 0 || o.band_rows > dev::kBandRows)
             throw StatusError(VCSRMC_INVALID_ARG, "band_rows must be 0 or in [1, 128]");
+        check_hot_options(o);
         if (device < 0) cuda_check(cudaGetDevice(&device), "cudaGetDevice");
         DeviceGuard guard(device);
         cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -606,6 +710,7 @@ VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const i
             }
             if (!dev::device_validate(d->has_segment ? &seg : nullptr, d->has_rows ? &rows : nullptr, M, N, segw, st))
                 throw StatusError(VCSRMC_INTERNAL, "device-built format failed its index checks");
+            make_hot_columns(d, nnz, o, st);
             if (plans & (1 << VCSRMC_PLAN_BAND)) {
                 dev::BandLayout band = dev::build_band_layout(row_ptr, col, val, M, nnz, scale, band_rows, st);
                 d->band_rows = band.band_rows;

@@ -19,6 +19,11 @@
 // the unit's row ends and a ballot marks the last entry of every row.
 // A values and column indices are streamed (evict-first); B keeps the default caching so hot
 // columns stay in L1/L2.
+// Hot columns: the row view may number its most used columns by rank (entries hold ~rank, see
+// RowHotView). Each call then first copies the B rows of the leading ranks into one compact
+// buffer (hot_rows_copy_kernel), optionally under a persisting L2 access-policy window, and an
+// entry's B row is read from there. The values read and the order of the FMAs are the same as
+// without the copy, so C is bit-identical either way.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -76,6 +81,14 @@ __device__ __forceinline__ uint4 load16(const BT* p, int nv) {
         for (int i = 0; i < nv; ++i) w[i] = q[i];
     }
     return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Same, for a B row read once in a while: evict-first in L1 and L2 (ld.global.cs), so that it does not
+// displace the popular rows.
+template <bool kVec, typename BT>
+__device__ __forceinline__ uint4 load16_once(const BT* p, int nv) {
+    if (kVec && nv == Lane16<BT>::kElems) return __ldcs(reinterpret_cast<const uint4*>(p));
+    return load16<false>(p, nv);
 }
 
 // acc[i] += a * B_lane[i]. fp16 x fp16 uses the mixed-precision FMA (f16 inputs, f32 accumulate:
@@ -157,6 +170,24 @@ __device__ __forceinline__ void write_lane(float* dst, const float (&acc)[8], fl
     }
 }
 
+// An entry as the gather loop reads it from shared memory: the byte offset of its B row (relative
+// to B, or to the compact hot rows through hot_delta) and its A value bits.
+struct alignas(16) Staged {
+    long long off;
+    uint32_t v;
+    uint32_t once;  // 1: a row outside the hot set, read with evict-first
+};
+
+// Where a row-view entry's B row is: column c >= 0 is row c of B; a hot entry (~rank) below k_copy
+// is row `rank` of the compact copy (hot_delta = copy - B, in bytes); other hot ranks are looked up.
+__device__ __forceinline__ long long entry_offset(int c, int row_bytes, const int* __restrict__ hot_cols, int k_copy,
+                                                 long long hot_delta) {
+    if (c >= 0) return (long long)c * row_bytes;
+    const int r = ~c;
+    if (r < k_copy) return hot_delta + (long long)r * row_bytes;
+    return (long long)__ldg(hot_cols + r) * row_bytes;
+}
+
 constexpr int kInFlight = VCSRMC_ROWS_IN_FLIGHT;  // B gathers in flight per lane
 static_assert(kInFlight == 8 || kInFlight == 16, "a batch of 16 entries in rounds of 8 or 16");
 
@@ -170,16 +201,17 @@ template <bool kVec, bool kAccumulate, typename VT, typename BT>
 __global__ void VCSRMC_ROWS_BOUNDS
     vcsr_rows_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
                      const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
-                     int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale) {
+                     int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale,
+                     const int* __restrict__ hot_cols, int k_copy, long long hot_delta, int cold_hint) {
     constexpr int kE = Lane16<BT>::kElems;
     constexpr int kL = Lane16<BT>::kLanes;
     constexpr int kGroups = 32 / kL;
     constexpr RowOut kOut = kAccumulate ? RowOut::kAdd : RowOut::kStore;
-    __shared__ int2 stage_all[kWarpsPerBlock * 32];
+    __shared__ Staged stage_all[kWarpsPerBlock * 32];
     const int lane = threadIdx.x & 31;
     const int sub = lane / kL, sl = lane % kL;
     const unsigned gmask = kL == 32 ? kFull : (0xffffu << (16 * sub));
-    int2* stage = stage_all + (threadIdx.x >> 5) * 32 + sub * kL;
+    Staged* stage = stage_all + (threadIdx.x >> 5) * 32 + sub * kL;
     const int64_t unit = (int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5)) * kGroups + sub;
     if (unit >= n_units) return;  // the whole group leaves together
     const int4 u = units[unit];
@@ -217,7 +249,7 @@ __global__ void VCSRMC_ROWS_BOUNDS
     }
     for (int q = pb; q < pe; q += kL) {
         const int n = min(kL, pe - q);
-        stage[sl] = make_int2(mc, int(mv));
+        stage[sl] = Staged{entry_offset(mc, row_bytes, hot_cols, k_copy, hot_delta), mv, uint32_t(cold_hint & (mc >= 0))};
         mc = 0;
         mv = 0;
         if (q + kL + sl < pe) {
@@ -245,9 +277,10 @@ __global__ void VCSRMC_ROWS_BOUNDS
             uint32_t av[kInFlight];
 #pragma unroll
             for (int k = 0; k < kInFlight; ++k) {
-                const int2 e = stage[j + k];
-                av[k] = uint32_t(e.y);
-                raw[k] = load16<kVec>(reinterpret_cast<const BT*>(bbase + int64_t(e.x) * row_bytes), nv);
+                const Staged e = stage[j + k];
+                av[k] = e.v;
+                const BT* p = reinterpret_cast<const BT*>(bbase + e.off);
+                raw[k] = e.once ? load16_once<kVec>(p, nv) : load16<kVec>(p, nv);
             }
             const unsigned eb = (ends >> j) & ((1u << kInFlight) - 1u);
             if (eb == 0) {
@@ -282,7 +315,8 @@ template <int kF, bool kVec, bool kAccumulate, typename VT, typename BT>
 __global__ void __launch_bounds__(kFoldedWarpsPerBlock * 32)
     vcsr_rows_folded_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
                             const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
-                            int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale) {
+                            int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale,
+                            const int* __restrict__ hot_cols, int k_copy, long long hot_delta, int cold_hint) {
     constexpr int kE = Lane16<BT>::kElems;
     constexpr int kL = Lane16<BT>::kLanes;
     constexpr int kW = kL / kF;        // lanes per entry
@@ -291,12 +325,12 @@ __global__ void __launch_bounds__(kFoldedWarpsPerBlock * 32)
     constexpr int kGroups = 32 / kL;
     constexpr RowOut kOut = kAccumulate ? RowOut::kAdd : RowOut::kStore;
     static_assert(kF == 2 || kF == 4, "fold of 2 or 4 entries");
-    __shared__ int2 stage_all[kFoldedWarpsPerBlock * 32];
+    __shared__ Staged stage_all[kFoldedWarpsPerBlock * 32];
     const int lane = threadIdx.x & 31;
     const int sub = lane / kL, sl = lane % kL;
     const int fold = sl / kW, cl = sl % kW;
     const unsigned gmask = kL == 32 ? kFull : (0xffffu << (16 * sub));
-    int2* stage = stage_all + (threadIdx.x >> 5) * 32 + sub * kL;
+    Staged* stage = stage_all + (threadIdx.x >> 5) * 32 + sub * kL;
     const int64_t unit = (int64_t(blockIdx.x) * kFoldedWarpsPerBlock + (threadIdx.x >> 5)) * kGroups + sub;
     if (unit >= n_units) return;  // the whole group leaves together
     const int4 u = units[unit];
@@ -331,7 +365,7 @@ __global__ void __launch_bounds__(kFoldedWarpsPerBlock * 32)
     }
     for (int q = pb; q < pe; q += kL) {
         const int n = min(kL, pe - q);
-        stage[sl] = make_int2(mc, int(mv));
+        stage[sl] = Staged{entry_offset(mc, row_bytes, hot_cols, k_copy, hot_delta), mv, uint32_t(cold_hint & (mc >= 0))};
         mc = 0;
         mv = 0;
         if (q + kL + sl < pe) {
@@ -357,9 +391,10 @@ __global__ void __launch_bounds__(kFoldedWarpsPerBlock * 32)
             uint32_t av[kR];
 #pragma unroll
             for (int k = 0; k < kR; ++k) {
-                const int2 e = stage[(t0 + k) * kF + fold];
-                av[k] = uint32_t(e.y);
-                raw[k] = load16<kVec>(reinterpret_cast<const BT*>(bbase + int64_t(e.x) * row_bytes), nv);
+                const Staged e = stage[(t0 + k) * kF + fold];
+                av[k] = e.v;
+                const BT* p = reinterpret_cast<const BT*>(bbase + e.off);
+                raw[k] = e.once ? load16_once<kVec>(p, nv) : load16<kVec>(p, nv);
             }
 #pragma unroll
             for (int k = 0; k < kR; ++k) {
@@ -408,6 +443,58 @@ __global__ void zero_rows_kernel(const int* __restrict__ rows, int n_rows, int O
     for (int c = threadIdx.x; c < O; c += blockDim.x) dst[c] = 0.f;
 }
 
+// Copies the B rows of hot ranks 0 .. k-1 into `dst` (row r of dst = B row hot_cols[r], same row
+// pitch); only the first copy_bytes of each row (the O columns read) are copied. 16 lanes per row,
+// 16 bytes per lane when B's rows are 16-byte aligned, 2 bytes otherwise.
+__global__ void hot_rows_copy_kernel(const int* __restrict__ hot_cols, int k, const char* __restrict__ B,
+                                     int row_bytes, int copy_bytes, char* __restrict__ dst, int vec) {
+    const int64_t tid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t groups = int64_t(gridDim.x) * blockDim.x / 16;
+    const int sl = int(tid & 15);
+    const int vec_bytes = vec ? (copy_bytes & ~15) : 0;
+    for (int64_t r = tid >> 4; r < k; r += groups) {
+        const char* src = B + int64_t(__ldg(hot_cols + r)) * row_bytes;
+        char* d = dst + r * row_bytes;
+        for (int b = sl * 16; b < vec_bytes; b += 256)
+            *reinterpret_cast<uint4*>(d + b) = __ldg(reinterpret_cast<const uint4*>(src + b));
+        for (int b = vec_bytes + sl * 2; b < copy_bytes; b += 32)
+            *reinterpret_cast<unsigned short*>(d + b) = *reinterpret_cast<const unsigned short*>(src + b);
+    }
+}
+
+// Launch configuration of the plan's kernels, with the persisting L2 window over the compact hot
+// rows when that is asked for.
+struct LaunchShape {
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    LaunchShape(dim3 grid, dim3 block, cudaStream_t st, const void* window, int64_t window_bytes) {
+        cfg.gridDim = grid;
+        cfg.blockDim = block;
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = 0;
+        if (window && window_bytes > 0) {
+            int dev = 0, max_window = 0;
+            size_t persisting = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&max_window, cudaDevAttrMaxAccessPolicyWindowSize, dev);
+            cudaDeviceGetLimit(&persisting, cudaLimitPersistingL2CacheSize);
+            cudaGetLastError();
+            const int64_t bytes = std::min<int64_t>(window_bytes, max_window);
+            if (bytes > 0 && persisting > 0) {
+                attr[0].id = cudaLaunchAttributeAccessPolicyWindow;
+                attr[0].val.accessPolicyWindow.base_ptr = const_cast<void*>(window);
+                attr[0].val.accessPolicyWindow.num_bytes = size_t(bytes);
+                attr[0].val.accessPolicyWindow.hitRatio = float(std::min(1.0, double(persisting) / double(bytes)));
+                attr[0].val.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
+                attr[0].val.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
+                cfg.numAttrs = 1;
+            }
+        }
+    }
+};
+
 template <bool kVec, bool kAcc, typename VT, typename BT>
 cudaError_t launch_rows_t(const RowPlanView& P, const BT* B, int64_t ldb, int O, float* C, int64_t ldc,
                           cudaStream_t st) {
@@ -420,21 +507,45 @@ cudaError_t launch_rows_t(const RowPlanView& P, const BT* B, int64_t ldb, int O,
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
     const int row_bytes = int(ldb * int64_t(sizeof(BT)));
     const VT* vals = static_cast<const VT*>(P.vals);
+    // hot rows: copy the leading ranks' B rows into the compact buffer first
+    const int k_copy = rows_hot_copy_count(P.hot, row_bytes);
+    long long hot_delta = 0;
+    const void* window = nullptr;
+    int64_t window_bytes = 0;
+    if (k_copy > 0) {
+        int dev = 0, sms = 1;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int64_t copy_blocks = std::min<int64_t>((int64_t(k_copy) * 16 + 255) / 256, int64_t(sms) * 8);
+        if (P.hot.persist) {
+            window = P.hot.buf;
+            window_bytes = int64_t(k_copy) * row_bytes;
+        }
+        const int copy_vec = (reinterpret_cast<uintptr_t>(B) % 16 == 0) && (row_bytes % 16 == 0);
+        LaunchShape L(dim3(unsigned(copy_blocks)), dim3(256), st, window, window_bytes);
+        const cudaError_t e = cudaLaunchKernelEx(&L.cfg, hot_rows_copy_kernel, P.hot.hot_cols, k_copy,
+                                                 reinterpret_cast<const char*>(B), row_bytes,
+                                                 int(O * int64_t(sizeof(BT))), static_cast<char*>(P.hot.buf), copy_vec);
+        if (e != cudaSuccess) return e;
+        hot_delta = static_cast<const char*>(P.hot.buf) - reinterpret_cast<const char*>(B);
+    }
+    const int* hot_cols = P.hot.hot_cols;
+    const int cold_hint = (P.hot.n_hot > 0 && P.hot.cold_hint) ? 1 : 0;
     // narrow B: fold 4 or 2 entries into one lane group when a row slice fits a quarter or half
     if (O <= kL * kE / 4) {
-        vcsr_rows_folded_kernel<4, kVec, kAcc, VT, BT><<<unsigned(fblocks), kFoldedWarpsPerBlock * 32, 0, st>>>(
-            P.units, P.n_units, P.rp, P.cols, vals, B, row_bytes, O, C, ldc, P.scale);
-        return cudaGetLastError();
+        LaunchShape L(dim3(unsigned(fblocks)), dim3(kFoldedWarpsPerBlock * 32), st, window, window_bytes);
+        return cudaLaunchKernelEx(&L.cfg, vcsr_rows_folded_kernel<4, kVec, kAcc, VT, BT>, P.units, P.n_units, P.rp,
+                                  P.cols, vals, B, row_bytes, O, C, ldc, P.scale, hot_cols, k_copy, hot_delta, cold_hint);
     }
     if (O <= kL * kE / 2) {
-        vcsr_rows_folded_kernel<2, kVec, kAcc, VT, BT><<<unsigned(fblocks), kFoldedWarpsPerBlock * 32, 0, st>>>(
-            P.units, P.n_units, P.rp, P.cols, vals, B, row_bytes, O, C, ldc, P.scale);
-        return cudaGetLastError();
+        LaunchShape L(dim3(unsigned(fblocks)), dim3(kFoldedWarpsPerBlock * 32), st, window, window_bytes);
+        return cudaLaunchKernelEx(&L.cfg, vcsr_rows_folded_kernel<2, kVec, kAcc, VT, BT>, P.units, P.n_units, P.rp,
+                                  P.cols, vals, B, row_bytes, O, C, ldc, P.scale, hot_cols, k_copy, hot_delta, cold_hint);
     }
-    const dim3 grid(unsigned(blocks), unsigned((O + 127) / 128));
-    vcsr_rows_kernel<kVec, kAcc, VT, BT><<<grid, kWarpsPerBlock * 32, 0, st>>>(
-        P.units, P.n_units, P.rp, P.cols, vals, B, row_bytes, O, C, ldc, P.scale);
-    return cudaGetLastError();
+    LaunchShape L(dim3(unsigned(blocks), unsigned((O + 127) / 128)), dim3(kWarpsPerBlock * 32), st, window,
+                  window_bytes);
+    return cudaLaunchKernelEx(&L.cfg, vcsr_rows_kernel<kVec, kAcc, VT, BT>, P.units, P.n_units, P.rp, P.cols, vals, B,
+                              row_bytes, O, C, ldc, P.scale, hot_cols, k_copy, hot_delta, cold_hint);
 }
 
 template <typename VT, typename BT>
@@ -453,6 +564,18 @@ cudaError_t launch_rows_b(const RowPlanView& P, const BT* B, int64_t ldb, int O,
 }
 
 }  // namespace
+
+int rows_hot_copy_count(const RowHotView& H, int64_t row_bytes) {
+    if (!H.buf || H.n_hot <= 0 || H.budget_bytes <= 0 || row_bytes <= 0) return 0;
+    const int64_t cap = std::min(H.budget_bytes, H.buf_bytes) / row_bytes;
+    return int(std::min<int64_t>(H.n_hot, cap));
+}
+
+int rows_launch_count(const RowPlanView& P, int64_t ldb, int b_is_f16, int O, bool accumulate) {
+    if (P.n_units == 0 || O == 0) return 0;
+    const int64_t row_bytes = ldb * (b_is_f16 ? 2 : 4);
+    return (!accumulate && P.n_split_rows > 0 ? 1 : 0) + (rows_hot_copy_count(P.hot, row_bytes) > 0 ? 1 : 0) + 1;
+}
 
 cudaError_t spmm_rows(const RowPlanView& P, const void* B, int b_is_f16, int64_t ldb, int O, float* C, int64_t ldc,
                       bool accumulate, cudaStream_t st) {
