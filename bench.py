@@ -63,6 +63,9 @@ def workload_spec(name: str, scale: int) -> dict:
         return {"kind": vm.GEN_ZIPF, "param": 262144, "desc": "config2 262144^2 Zipf(1.8) mean 10 cap 8192"}
     if name == "c3":
         return {"kind": vm.GEN_STENCIL27, "param": 100, "desc": "config3 27-point stencil 100^3"}
+    if name == "c3links":
+        return {"kind": vm.GEN_STENCIL27_LINKS, "param": 100,
+                "desc": "27-point stencil 100^3 plus 3 random long-range links per row (not a BASELINE config)"}
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -290,15 +293,18 @@ def shard_balance(args, spec: dict, fp16: bool) -> None:
     import vcsr_mc_b200 as vm
     M, N, rp, col, val = load_or_generate_csr(spec, 0, 1, lambda: None)
     rp32 = np.asarray(rp, dtype=np.int32)
-    plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND}[args.plan]
+    plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND, "hybrid": vm.PLAN_HYBRID}[args.plan]
     B = torch.empty((N, O_COLS), dtype=torch.float16 if fp16 else torch.float32, device="cuda")
     vm.gen_dense_device(B, SEED)
 
     def shard_ms(r0: int, r1: int) -> float:
         p0, p1 = int(rp[r0]), int(rp[r1])
-        S = vm.CSR.from_arrays(r1 - r0, N, np.asarray(rp[r0:r1 + 1], dtype=np.int64) - p0,
-                               np.asarray(col[p0:p1]), np.asarray(val[p0:p1]))
-        dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(S, fp32=not fp16, segw=args.segw), device=0, plans=[plan])
+        d_rp = torch.from_numpy(np.asarray(rp[r0:r1 + 1], dtype=np.int64) - p0).to(torch.int32).cuda()
+        d_col = torch.from_numpy(np.asarray(col[p0:p1])).cuda()
+        d_val = torch.from_numpy(np.asarray(val[p0:p1])).cuda()
+        dV = vm.build_vcsr_mc_device(d_rp, d_col, d_val, r1 - r0, N, fp32=not fp16, segw=args.segw, device=0,
+                                     plans=[plan])
+        del d_rp, d_col, d_val
         C = torch.empty((max(r1 - r0, 1), O_COLS), dtype=torch.float32, device="cuda")
         for _ in range(args.warmup):
             vm.spmm(dV, B, C, tileK=args.tileK, plan=plan)
@@ -338,12 +344,12 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["rmat", "c1", "c2", "c3"], default="rmat")
+    ap.add_argument("--workload", choices=["rmat", "c1", "c2", "c3", "c3links"], default="rmat")
     ap.add_argument("--scale", type=int, default=24)
     ap.add_argument("--dtype", choices=["fp16", "fp32"], default="fp16")
     ap.add_argument("--segw", type=int, default=32)
     ap.add_argument("--tileK", type=int, default=128)
-    ap.add_argument("--plan", choices=["rows", "segment", "band"], default="rows")
+    ap.add_argument("--plan", choices=["rows", "segment", "band", "hybrid"], default="rows")
     ap.add_argument("--e2e-steps", type=int, default=12)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -369,7 +375,7 @@ def main() -> None:
                     help="e.g. 2,4,8: time every shard of each N-way row partition one after another on this "
                          "GPU (the path has no collective, so the slowest shard predicts the N-GPU step) and "
                          "print that instead of the bench line")
-    ap.add_argument("--row-weights", default="0,3,5.4,8", help="row weights tried by --shard-balance")
+    ap.add_argument("--row-weights", default="0,3,3.8,5.4", help="row weights tried by --shard-balance")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.row_weight is None:
@@ -386,7 +392,9 @@ def main() -> None:
                        ("CUDA-core FFMA" if (args.plan == "rows" or not fp16) else "tcgen05 MMA, TMEM accumulator")),
               "plan": {"rows": "rows: row-stationary over the VCSR-MC row view, C stored once",
                        "segment": "segment: reference dataflow, per-item B segment, C reductions",
-                       "band": "band: 128-row bands x {band_cols}-column tiles on tcgen05, TMEM accumulator, C stored once"}[args.plan],
+                       "band": "band: 128-row bands x {band_cols}-column tiles on tcgen05, TMEM accumulator, C stored once",
+                       "hybrid": "hybrid: band tiles with >= 64 entries on tcgen05 (C stored once), the other entries "
+                                 "on the rows plan added into C"}[args.plan],
               "parallelism": f"row-shard x{args.gpus} (balanced on nnz + {args.row_weight} x rows), B replicated",
               "l2": None}
 
@@ -441,7 +449,9 @@ def main() -> None:
     shard = vm.CSR.from_arrays(r1 - r0, N, np.asarray(rp[r0:r1 + 1], dtype=np.int64) - p0,
                                np.asarray(col[p0:p1]), np.asarray(val[p0:p1]))
     nthreads = max(1, cores // world)
-    plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND}[args.plan]
+    plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND, "hybrid": vm.PLAN_HYBRID}[args.plan]
+    if plan == vm.PLAN_HYBRID and args.build == "device":
+        args.build = "host"  # the hybrid layout is made by an upload
     hot = {"hot_rows": args.hot_rows, "hot_budget_mib": args.hot_budget_mib, "hot_persist": args.hot_persist,
            "hot_evict_first": args.hot_evict_first}
     torch.cuda.synchronize()
@@ -465,7 +475,8 @@ def main() -> None:
     info = dV.info()
     # this library's kernels per step: the SpMM kernel, plus (ROWS plan) the zeroing of the rows
     # split into chunks that are reduced into C
-    launches_per_step = 1 + (1 if plan == vm.PLAN_ROWS and info["n_split_rows"] > 0 else 0) + \
+    launches_per_step = (2 if plan == vm.PLAN_HYBRID and info["hybrid_rows_nnz"] > 0 else 1) + \
+        (1 if plan == vm.PLAN_ROWS and info["n_split_rows"] > 0 else 0) + \
         (1 if plan == vm.PLAN_ROWS and info["n_hot"] > 0 and args.hot_budget_mib > 0 else 0)
     groups, slots, items = info["n_groups"], info["n_slots"], info["n_items"]
     config["plan"] = config["plan"].format(band_cols=info["band_cols"])
@@ -714,7 +725,7 @@ def main() -> None:
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
                                            "(profiles/measured_traffic.json)" if traffic else None,
-                         "kernel": {"rows": "vcsr_rows_kernel", "band": "vcsr_band_kernel",
+                         "kernel": {"rows": "vcsr_rows_kernel", "band": "vcsr_band_kernel", "hybrid": "vcsr_band_kernel",
                                     "segment": "vcsr_mc_fp16_tc_kernel" if fp16 else "vcsr_mc_fp32_kernel"}[args.plan],
                          "kernel_ms": kern_ms, "kernel_ms_max_over_ranks": kern_max_ms,
                          "algorithmic_bytes": bytes_alg},

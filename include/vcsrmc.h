@@ -50,17 +50,24 @@ extern "C" {
  * BAND:    FP16 format only: bands of <= 128 rows, tiles of 64 columns multiplied on the tensor
  *          cores into one accumulator per band, C stored once. For matrices whose rows touch
  *          few column windows (stencils, banded or reordered matrices).
- * AUTO:    the first resident layout of BAND (fp16 B only), ROWS, SEGMENT, BAND.          */
+ * HYBRID:  FP16 format only: the band tiles that hold at least 64 entries run as BAND (C written
+ *          once), every other entry then runs on ROWS, added into C. For matrices with dense
+ *          blocks and scattered entries. Built by an upload (vcsrmc_upload_ex), not on the GPU.
+ * AUTO:    the first resident layout of BAND (fp16 B only), HYBRID (fp16 B only), ROWS,
+ *          SEGMENT, BAND, HYBRID.                                                           */
 #define VCSRMC_PLAN_AUTO 0
 #define VCSRMC_PLAN_SEGMENT 1
 #define VCSRMC_PLAN_ROWS 2
 #define VCSRMC_PLAN_BAND 3
+#define VCSRMC_PLAN_HYBRID 4
 
 /* ---- synthetic configurations (vcsrmc_gen_csr) ---------------------------------------- */
 #define VCSRMC_GEN_UNIFORM_POISSON 1 /* param: M = N; mean row length 16                   */
 #define VCSRMC_GEN_ZIPF 2            /* param: M = N; Zipf(1.8) lengths, mean 10, cap 8192  */
 #define VCSRMC_GEN_STENCIL27 3       /* param: grid edge n (n^3 rows)                       */
 #define VCSRMC_GEN_RMAT 4            /* param: scale (2^scale rows); 2^(scale+4) samples     */
+#define VCSRMC_GEN_STENCIL27_LINKS 5 /* param: grid edge n; the 27-point stencil plus 3 random
+                                        long-range links per row (no reference counterpart)  */
 
 typedef struct vcsrmc_csr vcsrmc_csr;                     /* host CSR                    */
 typedef struct vcsrmc_format vcsrmc_format;               /* host VCSR-MC format         */
@@ -140,9 +147,10 @@ void vcsrmc_format_free(vcsrmc_format* f);
  * the device). Blocking. */
 int vcsrmc_upload(const vcsrmc_format* f, int device, void* stream, vcsrmc_device_format** out);
 /* Same, choosing which plan layouts to make resident: a bit mask of (1 << VCSRMC_PLAN_SEGMENT),
- * (1 << VCSRMC_PLAN_ROWS) and (1 << VCSRMC_PLAN_BAND). 0 (what vcsrmc_upload does) = SEGMENT and
- * ROWS, plus BAND for an FP16 format whose band x 64-column tiles hold enough entries to
- * beat ROWS (estimated from a sample of bands). */
+ * (1 << VCSRMC_PLAN_ROWS), (1 << VCSRMC_PLAN_BAND) and (1 << VCSRMC_PLAN_HYBRID). 0 (what
+ * vcsrmc_upload does) = SEGMENT and ROWS, plus, for an FP16 format, BAND where its band x 64-column
+ * tiles hold enough entries on average to beat ROWS, else HYBRID where at least half the entries
+ * sit in tiles that dense (both estimated from a sample of bands). */
 int vcsrmc_upload_ex(const vcsrmc_format* f, int device, int plans, void* stream,
                      vcsrmc_device_format** out);
 /* Upload tuning; zero-initialise and set what you need (0 = the library's choice). */
@@ -206,6 +214,10 @@ typedef struct {
     int64_t n_tiles;
     int32_t band_cols;                    /* BAND: columns per tile (this build's tile width) */
     int32_t n_hot;                        /* ROWS: ranked hot columns (0: none)              */
+    int32_t hybrid_band_rows, reserved2;  /* HYBRID: rows per band of its band part          */
+    int64_t hybrid_tiles;                 /* HYBRID: dense tiles                             */
+    int64_t hybrid_band_nnz;              /* HYBRID: entries run on the tensor cores         */
+    int64_t hybrid_rows_nnz;              /* HYBRID: entries run on the rows plan            */
 } vcsrmc_device_info;
 int vcsrmc_device_info_get(const vcsrmc_device_format* d, vcsrmc_device_info* out);
 /* Error flags raised by kernels of this format since the last clear (bit 0: a bounded wait

@@ -26,6 +26,12 @@ VCSRMC_CXX_API double zipf_length_factor(double s, int kmax, double mean);
 // off-diagonal -1 + U(-0.01, 0.01).
 VCSRMC_CXX_API CSR gen_stencil27(int nx, int ny, int nz, uint64_t seed, int nthreads = 0);
 
+// The 27-point stencil of gen_stencil27 on n^3 plus `links` long-range links per row: link t of
+// row i joins column (draw 2 (i links + t) of the links stream) mod n^3 with value U(-1,1) (the
+// next draw); a link that falls on a stencil column or an earlier link of the row is dropped. A
+// stand-in for a finite-element matrix with far couplings: dense diagonal bands plus scatter.
+VCSRMC_CXX_API CSR gen_stencil27_links(int n, int links, uint64_t seed, int nthreads = 0);
+
 // R-MAT graph with 2^scale vertices: `edges` samples with quadrant probabilities
 // (a, b, c, 1-a-b-c), duplicates removed, values U(-1,1).
 VCSRMC_CXX_API CSR gen_rmat(int scale, int64_t edges, double a, double b, double c, uint64_t seed, int nthreads = 0);

@@ -126,6 +126,31 @@ void check_units(const std::vector<int>& rp, int M, int u) {
     expect(next == M, "light runs cover every light row", next, M);
 }
 
+// skip_empty: the same heavy-row chunks; light runs never start at an empty row, and every
+// non-empty light row is in exactly one run (empty rows may sit inside a run).
+void check_units_skip_empty(const std::vector<int>& rp, int M, int u) {
+    std::vector<RowViewHost::Unit> units;
+    std::vector<int> split;
+    pack_units(rp.data(), M, u, units, split, true);
+    auto len = [&](int r) { return rp[size_t(r) + 1] - rp[size_t(r)]; };
+    std::vector<int> covered(size_t(std::max(M, 1)), 0);
+    for (const auto& t : units) {
+        if (t.y & 0x80000000) continue;  // heavy-row chunk (checked by check_units)
+        expect(len(t.x) > 0, "no run starts at an empty row", t.x, 0);
+        expect(t.y > t.x && t.y - t.x <= kUnitRows && t.y <= M, "run of 1 .. kUnitRows rows", t.x, t.y);
+        expect(t.z == rp[size_t(t.x)] && t.w == rp[size_t(t.y)], "run entry range", t.z, t.w);
+        int n = 0;
+        for (int r = t.x; r < t.y; ++r) {
+            expect(len(r) <= u, "run holds only light rows", r, len(r));
+            n += len(r);
+            ++covered[size_t(r)];
+        }
+        expect(n <= u, "run within unit_nnz entries", n, u);
+    }
+    for (int r = 0; r < M; ++r)
+        if (len(r) > 0 && len(r) <= u) expect(covered[size_t(r)] == 1, "non-empty light row in exactly one run", r, covered[size_t(r)]);
+}
+
 void check_row_view(const Csr& a, bool fp32, int segw, int u) {
     vcsrmc::CSR c;
     c.M = a.M;
@@ -202,6 +227,54 @@ void check_band(const Csr& a, int H) {
     }
 }
 
+// Hybrid split: the dense and residual row views partition every row's entries (each in ascending
+// column order, together the row), the dense ones are exactly the entries of tiles holding at
+// least min_entries entries, and the band view of the dense part has exactly those tiles.
+void check_hybrid_split(const Csr& a, int H, int min_entries) {
+    RowViewHost rv;
+    rv.rp = a.rp;
+    rv.cols = a.col;
+    rv.vals = a.val;
+    const BandViewHost bv = build_band_view(rv, a.M, H, 2);
+    RowViewHost dense, resid;
+    split_dense_tiles(rv, bv, a.M, min_entries, 2, dense, resid);
+    std::vector<int> want_cols;  // tile columns of the dense tiles, in order
+    std::vector<int> want_n;
+    long long dense_nnz = 0;
+    for (size_t t = 0; t + 1 < bv.tile_eptr.size(); ++t) {
+        const int n = bv.tile_eptr[t + 1] - bv.tile_eptr[t];
+        if (n >= min_entries) {
+            want_cols.push_back(bv.tile_col[t]);
+            want_n.push_back(n);
+            dense_nnz += n;
+        }
+    }
+    expect(ll(dense.cols.size()) == dense_nnz, "dense part holds the dense tiles' entries", ll(dense.cols.size()), dense_nnz);
+    expect(dense.cols.size() + resid.cols.size() == a.col.size(), "the split keeps every entry", ll(dense.cols.size()),
+           ll(resid.cols.size()));
+    for (int r = 0; r < a.M; ++r) {
+        std::vector<std::pair<int, float>> merged;
+        for (int p = dense.rp[size_t(r)]; p < dense.rp[size_t(r) + 1]; ++p) {
+            expect(p == dense.rp[size_t(r)] || dense.cols[size_t(p)] > dense.cols[size_t(p) - 1], "dense row ascending", r, p);
+            merged.push_back({dense.cols[size_t(p)], dense.vals[size_t(p)]});
+        }
+        for (int p = resid.rp[size_t(r)]; p < resid.rp[size_t(r) + 1]; ++p) {
+            expect(p == resid.rp[size_t(r)] || resid.cols[size_t(p)] > resid.cols[size_t(p) - 1], "residual row ascending", r, p);
+            merged.push_back({resid.cols[size_t(p)], resid.vals[size_t(p)]});
+        }
+        std::sort(merged.begin(), merged.end(), [](auto x, auto y) { return x.first < y.first; });
+        bool same = merged.size() == size_t(a.rp[size_t(r) + 1] - a.rp[size_t(r)]);
+        for (size_t i = 0; same && i < merged.size(); ++i)
+            same = merged[i].first == a.col[size_t(a.rp[size_t(r)]) + i] && merged[i].second == a.val[size_t(a.rp[size_t(r)]) + i];
+        expect(same, "dense and residual rows together are the row", r, H);
+    }
+    const BandViewHost dv = build_band_view(dense, a.M, H, 2);
+    std::vector<int> got_n;
+    for (size_t t = 0; t + 1 < dv.tile_eptr.size(); ++t) got_n.push_back(dv.tile_eptr[t + 1] - dv.tile_eptr[t]);
+    expect(dv.tile_col == want_cols && got_n == want_n, "the dense part's band view has exactly the dense tiles",
+           ll(dv.tile_col.size()), ll(want_cols.size()));
+}
+
 }  // namespace
 
 int main() {
@@ -218,6 +291,7 @@ int main() {
         }
         for (int u : {16, 64, 256, 1024}) {
             check_units(rp, M, u);
+            check_units_skip_empty(rp, M, u);
             ++n_units_checked;
         }
     }
@@ -232,6 +306,7 @@ int main() {
         }
         for (int H : {1, 37, 64, 112, 128}) {
             check_band(a, H);
+            for (int min_entries : {1, 8, 64}) check_hybrid_split(a, H, min_entries);
             ++n_bands_checked;
         }
         check_row_view(a, trial % 2 == 0, trial % 4 < 2 ? 16 : 32, trial % 3 == 0 ? 64 : 16);

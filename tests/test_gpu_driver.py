@@ -19,8 +19,11 @@ def run_driver(*args):
 
 
 @pytest.mark.parametrize("extra", [[], ["--plan", "segment"], ["--plan", "rows", "--b16"], ["--plan", "band", "--b16"],
-                                   ["--reorder", "rcm"], ["--bdist", "wide", "--segw", "32", "--tileK", "128"]],
-                         ids=["reference-call", "segment", "rows-b16", "band-b16", "rcm", "wide-s32-t128"])
+                                   ["--plan", "hybrid", "--b16"], ["--reorder", "rcm"],
+                                   ["--bdist", "wide", "--segw", "32", "--tileK", "128"],
+                                   ["--flush-l2", "--peak-gbs", "6545.3"]],
+                         ids=["reference-call", "segment", "rows-b16", "band-b16", "hybrid-b16", "rcm", "wide-s32-t128",
+                              "flush-roofline"])
 def test_driver_all_algorithms_pass(extra):
     rows = run_driver("--gen", "c1", "--algo", "all", "--repeat", "2", "--warmup", "1", *extra)
     algos = {r["algo"]: r for r in rows}
@@ -28,6 +31,8 @@ def test_driver_all_algorithms_pass(extra):
     for name, r in algos.items():
         assert r["validation"] == "pass", (name, r)
         assert float(r["gflops"]) > 0
+        assert float(r["gbps_alg"]) > 0
+        assert (r["roofline_frac"] != "") == ("--peak-gbs" in extra)
 
 
 def test_driver_mtx_input(tmp_path):

@@ -265,8 +265,32 @@ def test_config1_generator_matches_numpy_restatement():
     assert np.array_equal(val, rng.sym(rng.at(kvals, np.arange(exp[-1]))))
 
 
+def test_stencil_links_generator_matches_numpy_restatement():
+    """The stencil-plus-links generator: the stencil of GEN_STENCIL27 plus, per row, the columns of
+    the links stream that are not already in the row, each with the stream's next draw as value."""
+    from vcsr_mc_b200 import rng
+    n, links = 9, 3
+    A = vm.CSR.generate(vm.GEN_STENCIL27_LINKS, n, seed=4)
+    S = vm.CSR.generate(vm.GEN_STENCIL27, n, seed=4)
+    rp, col, val = A.arrays()
+    srp, scol, sval = S.arrays()
+    M = n ** 3
+    kl = rng.key(4, rng.STREAM_LINKS)
+    for r in range(M):
+        want = dict(zip(scol[srp[r]:srp[r + 1]].tolist(), sval[srp[r]:srp[r + 1]].tolist()))
+        d = 2 * (r * links + np.arange(links, dtype=np.uint64))
+        cs = (rng.at(kl, d) % np.uint64(M)).astype(np.int64)
+        vs = rng.sym(rng.at(kl, d + np.uint64(1)))
+        for c, v in zip(cs.tolist(), vs.tolist()):
+            if c not in want:
+                want[c] = v
+        cols = sorted(want)
+        assert col[rp[r]:rp[r + 1]].tolist() == cols, r
+        assert np.array_equal(val[rp[r]:rp[r + 1]], np.array([want[c] for c in cols], dtype=np.float32)), r
+
+
 def test_generators_deterministic_and_thread_independent():
-    for kind, param in [(vm.GEN_ZIPF, 4096), (vm.GEN_RMAT, 12), (vm.GEN_STENCIL27, 8)]:
+    for kind, param in [(vm.GEN_ZIPF, 4096), (vm.GEN_RMAT, 12), (vm.GEN_STENCIL27, 8), (vm.GEN_STENCIL27_LINKS, 8)]:
         a = vm.CSR.generate(kind, param, seed=1, nthreads=1).arrays()
         b = vm.CSR.generate(kind, param, seed=1, nthreads=5).arrays()
         for x, y in zip(a, b):

@@ -15,8 +15,8 @@ LIB_PATH = os.path.join(_HERE, "libvcsrmc.so")
 # status codes (vcsrmc.h)
 OK, INVALID_ARG, CUDA_ERR, OOM, TIMEOUT, IO_ERR, FORMAT_ERR, INTERNAL = range(8)
 F32, F16 = 0, 1
-GEN_UNIFORM_POISSON, GEN_ZIPF, GEN_STENCIL27, GEN_RMAT = 1, 2, 3, 4
-PLAN_AUTO, PLAN_SEGMENT, PLAN_ROWS, PLAN_BAND = 0, 1, 2, 3
+GEN_UNIFORM_POISSON, GEN_ZIPF, GEN_STENCIL27, GEN_RMAT, GEN_STENCIL27_LINKS = 1, 2, 3, 4, 5
+PLAN_AUTO, PLAN_SEGMENT, PLAN_ROWS, PLAN_BAND, PLAN_HYBRID = 0, 1, 2, 3, 4
 
 _STATUS_NAMES = {
     OK: "OK", INVALID_ARG: "INVALID_ARG", CUDA_ERR: "CUDA_ERR", OOM: "OOM", TIMEOUT: "TIMEOUT",
@@ -38,7 +38,9 @@ class DeviceInfo(ctypes.Structure):
                 ("n_groups", ctypes.c_int64), ("n_slots", ctypes.c_int64), ("n_items", ctypes.c_int64),
                 ("n_units", ctypes.c_int64), ("rows_unit_nnz", ctypes.c_int32), ("n_split_rows", ctypes.c_int32),
                 ("band_rows", ctypes.c_int32), ("n_bands", ctypes.c_int32),
-                ("n_tiles", ctypes.c_int64), ("band_cols", ctypes.c_int32), ("n_hot", ctypes.c_int32)]
+                ("n_tiles", ctypes.c_int64), ("band_cols", ctypes.c_int32), ("n_hot", ctypes.c_int32),
+                ("hybrid_band_rows", ctypes.c_int32), ("reserved2", ctypes.c_int32), ("hybrid_tiles", ctypes.c_int64),
+                ("hybrid_band_nnz", ctypes.c_int64), ("hybrid_rows_nnz", ctypes.c_int64)]
 
 
 class UploadOptions(ctypes.Structure):

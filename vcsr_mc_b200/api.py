@@ -20,7 +20,7 @@ from typing import Optional
 import numpy as np
 
 from . import _lib
-from ._lib import F16, F32, PLAN_AUTO, PLAN_BAND, PLAN_ROWS, PLAN_SEGMENT, VcsrmcError, call
+from ._lib import F16, F32, PLAN_AUTO, PLAN_BAND, PLAN_HYBRID, PLAN_ROWS, PLAN_SEGMENT, VcsrmcError, call
 
 
 def _ptr(a: np.ndarray) -> ctypes.c_void_p:
@@ -209,7 +209,7 @@ class DeviceVCSRMC:
         i = _lib.DeviceInfo()
         call("vcsrmc_device_info_get", self._h, ctypes.byref(i))
         out = {k: getattr(i, k) for k, _ in _lib.DeviceInfo._fields_}
-        out["plans"] = [p for p in (PLAN_SEGMENT, PLAN_ROWS, PLAN_BAND) if i.plans & (1 << p)]
+        out["plans"] = [p for p in (PLAN_SEGMENT, PLAN_ROWS, PLAN_BAND, PLAN_HYBRID) if i.plans & (1 << p)]
         return out
 
     def download(self) -> VCSRMC:
@@ -255,9 +255,9 @@ def _upload_options(plans, rows_unit_nnz: int, band_rows: int, hot_rows: int, ho
 def upload_vcsr_mc_device(V: VCSRMC, device: int = 0, stream=None, plans=None,
                           rows_unit_nnz: int = 0, band_rows: int = 0, hot_rows: int = 0, hot_budget_mib: int = 0,
                           hot_persist: int = 0, hot_evict_first: int = 0) -> DeviceVCSRMC:
-    """Copies the format to `device`. plans: iterable of PLAN_SEGMENT / PLAN_ROWS / PLAN_BAND
-    layouts to make resident (default: SEGMENT and ROWS, plus BAND for FP16 formats whose
-    column tiles are dense enough; BAND needs the FP16 format). rows_unit_nnz: entries per ROWS-plan work unit (0 = the library's
+    """Copies the format to `device`. plans: iterable of PLAN_SEGMENT / PLAN_ROWS / PLAN_BAND /
+    PLAN_HYBRID layouts to make resident (default: SEGMENT and ROWS, plus BAND for FP16 formats whose
+    column tiles are dense enough; BAND and HYBRID need the FP16 format). rows_unit_nnz: entries per ROWS-plan work unit (0 = the library's
     choice for this matrix). band_rows: rows per BAND-plan band, 1 .. 128 (0 = chosen).
     hot_rows / hot_budget_mib / hot_persist / hot_evict_first: the ROWS plan's hot columns, off by
     default (vcsrmc_upload_options)."""
@@ -344,9 +344,10 @@ def gen_dense_device(out, seed: int, stream=None):
 
 
 # Row weight of the multi-GPU partition that the benchmark and the sharded path use: a block's
-# cost is nnz + SHARD_ROW_WEIGHT * rows, from a fit of measured per-shard times of the ROWS plan on
-# the 2^24-row R-MAT (a per-entry cost plus a per-row cost, the C row store and the row bookkeeping).
-SHARD_ROW_WEIGHT = 5.4
+# cost is nnz + SHARD_ROW_WEIGHT * rows. It is the ratio of the per-row to the per-entry cost of the
+# ROWS plan fitted (least squares) to 56 measured shard times of the 2^24-row R-MAT: 0.118 ns per row
+# (the C row store and the row bookkeeping) against 0.0312 ns per entry.
+SHARD_ROW_WEIGHT = 3.8
 
 
 def partition_rows(row_ptr: np.ndarray, parts: int, row_weight: float = 0.0) -> np.ndarray:

@@ -254,6 +254,9 @@ VCSRMC_EXPORT int vcsrmc_gen_csr(int kind, int32_t param, uint64_t seed, int nth
                 case VCSRMC_GEN_STENCIL27:
                     h->csr = gen_stencil27(param, param, param, seed, nthreads);
                     break;
+                case VCSRMC_GEN_STENCIL27_LINKS:
+                    h->csr = gen_stencil27_links(param, 3, seed, nthreads);
+                    break;
                 case VCSRMC_GEN_RMAT:
                     if (param > 27) throw StatusError(VCSRMC_INVALID_ARG, "R-MAT scale > 27");
                     h->csr = gen_rmat(param, int64_t(1) << (param + 4), 0.57, 0.19, 0.19, seed, nthreads);

@@ -26,7 +26,8 @@ enum {
     VRNG_STREAM_COLS = 2,   /* column choice per row                         */
     VRNG_STREAM_VALS = 3,   /* values of A, indexed by CSR position          */
     VRNG_STREAM_DENSE = 4,  /* dense B, indexed by row * cols + col          */
-    VRNG_STREAM_RMAT = 5    /* R-MAT quadrant choices                        */
+    VRNG_STREAM_RMAT = 5,   /* R-MAT quadrant choices                        */
+    VRNG_STREAM_LINKS = 6   /* long-range links: column, value per link      */
 };
 
 VRNG_FN uint64_t vrng_mix64(uint64_t z) {

@@ -62,6 +62,22 @@ struct vcsrmc_device_format {
     int* tile_col = nullptr;
     int* tile_eptr = nullptr;
     uint32_t* ents = nullptr;
+    // HYBRID plan: the dense band tiles (a band view of their entries) and the other entries as a
+    // row view, run on the rows plan in accumulate mode after the band kernel
+    bool has_hybrid = false;
+    int hb_bands = 0, hb_rows = 0;
+    int64_t hb_tiles = 0, hb_nnz = 0;
+    int* hb_tile_ptr = nullptr;
+    int* hb_tile_col = nullptr;
+    int* hb_tile_eptr = nullptr;
+    uint32_t* hb_ents = nullptr;
+    int* hr_rp = nullptr;
+    int* hr_cols = nullptr;
+    void* hr_vals = nullptr;
+    int4* hr_units = nullptr;
+    int64_t hr_n_units = 0, hr_nnz = 0;
+    int* hr_split = nullptr;
+    int hr_n_split = 0;
     // ROWS plan, hot columns (RowHotView): ranked columns, and the compact copy of their B rows
     // that each call refreshes (grown on demand; launches of one handle are ordered).
     int* hot_cols = nullptr;
@@ -133,6 +149,15 @@ void free_device(vcsrmc_device_format* d) {
     cudaFree(d->tile_col);
     cudaFree(d->tile_eptr);
     cudaFree(d->ents);
+    cudaFree(d->hb_tile_ptr);
+    cudaFree(d->hb_tile_col);
+    cudaFree(d->hb_tile_eptr);
+    cudaFree(d->hb_ents);
+    cudaFree(d->hr_rp);
+    cudaFree(d->hr_cols);
+    cudaFree(d->hr_vals);
+    cudaFree(d->hr_units);
+    cudaFree(d->hr_split);
     cudaFree(d->hot_cols);
     cudaFree(d->hot_buf);
     // Lines marked persisting stay in L2's set-aside until reset and slow later kernels: return
@@ -265,17 +290,22 @@ void check_spmm_args(const vcsrmc_device_format* d, const void* B, int b_dtype, 
 int resolve_plan(const vcsrmc_device_format* d, int plan, int b_dtype) {
     if (plan == VCSRMC_PLAN_AUTO) {
         if (d->has_band && b_dtype == VCSRMC_F16) plan = VCSRMC_PLAN_BAND;
+        else if (d->has_hybrid && b_dtype == VCSRMC_F16) plan = VCSRMC_PLAN_HYBRID;
         else if (d->has_rows) plan = VCSRMC_PLAN_ROWS;
         else if (d->has_segment) plan = VCSRMC_PLAN_SEGMENT;
-        else plan = VCSRMC_PLAN_BAND;
+        else if (d->has_band) plan = VCSRMC_PLAN_BAND;
+        else plan = VCSRMC_PLAN_HYBRID;
     }
+    if (plan == VCSRMC_PLAN_HYBRID && !d->has_hybrid)
+        throw StatusError(VCSRMC_INVALID_ARG, "the HYBRID plan layout was not uploaded");
     if (plan == VCSRMC_PLAN_ROWS && !d->has_rows)
         throw StatusError(VCSRMC_INVALID_ARG, "the ROWS plan layout was not uploaded");
     if (plan == VCSRMC_PLAN_SEGMENT && !d->has_segment)
         throw StatusError(VCSRMC_INVALID_ARG, "the SEGMENT plan layout was not uploaded");
     if (plan == VCSRMC_PLAN_BAND && !d->has_band)
         throw StatusError(VCSRMC_INVALID_ARG, "the BAND plan layout was not uploaded");
-    if (plan != VCSRMC_PLAN_ROWS && plan != VCSRMC_PLAN_SEGMENT && plan != VCSRMC_PLAN_BAND)
+    if (plan != VCSRMC_PLAN_ROWS && plan != VCSRMC_PLAN_SEGMENT && plan != VCSRMC_PLAN_BAND &&
+        plan != VCSRMC_PLAN_HYBRID)
         throw StatusError(VCSRMC_INVALID_ARG, "unknown plan");
     return plan;
 }
@@ -307,6 +337,39 @@ void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int6
         P.hot.cold_hint = d->hot_evict_first;
         e = dev::spmm_rows(P, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, C, ldc, accumulate != 0, st);
         cuda_check(e, "SpMM launch (rows plan)");
+        return;
+    }
+    if (plan == VCSRMC_PLAN_HYBRID) {
+        // dense tiles on the tensor cores (every row of C written, or added to), then the other
+        // entries added by the rows plan
+        dev::BandPlanView P;
+        P.tile_ptr = d->hb_tile_ptr;
+        P.tile_col = d->hb_tile_col;
+        P.tile_eptr = d->hb_tile_eptr;
+        P.ents = d->hb_ents;
+        P.n_bands = d->hb_bands;
+        P.band_rows = d->hb_rows;
+        P.M = d->M;
+        P.N = d->N;
+        P.scale = d->scale;
+        P.status = d->status;
+        e = dev::spmm_band(P, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, C, ldc, accumulate != 0, st);
+        cuda_check(e, "SpMM launch (hybrid plan, band part)");
+        if (d->hr_nnz > 0) {
+            dev::RowPlanView R;
+            R.units = d->hr_units;
+            R.n_units = d->hr_n_units;
+            R.rp = d->hr_rp;
+            R.cols = d->hr_cols;
+            R.vals = d->hr_vals;
+            R.vals_f16 = 1;
+            R.split_rows = d->hr_split;
+            R.n_split_rows = d->hr_n_split;
+            R.M = d->M;
+            R.scale = d->scale;
+            e = dev::spmm_rows(R, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, C, ldc, true, st);
+            cuda_check(e, "SpMM launch (hybrid plan, rows part)");
+        }
         return;
     }
     if (plan == VCSRMC_PLAN_BAND) {
@@ -381,10 +444,12 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
         int plans = opts->plans;
         const bool default_plans = plans == 0;
         if (default_plans) plans = (1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS);
-        if (plans & ~((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS) | (1 << VCSRMC_PLAN_BAND)))
+        if (plans & ~((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS) | (1 << VCSRMC_PLAN_BAND) |
+                      (1 << VCSRMC_PLAN_HYBRID)))
             throw StatusError(VCSRMC_INVALID_ARG, "unknown plan bits");
-        if ((plans & (1 << VCSRMC_PLAN_BAND)) && f->v.fp32)
-            throw StatusError(VCSRMC_INVALID_ARG, "the BAND plan runs on the tensor cores and needs the FP16 format");
+        if ((plans & ((1 << VCSRMC_PLAN_BAND) | (1 << VCSRMC_PLAN_HYBRID))) && f->v.fp32)
+            throw StatusError(VCSRMC_INVALID_ARG,
+                              "the BAND and HYBRID plans run on the tensor cores and need the FP16 format");
         int unit_nnz = opts->rows_unit_nnz;
         if (unit_nnz != 0 && (unit_nnz < 16 || unit_nnz > dev::kUnitNnzMax || (unit_nnz & (unit_nnz - 1))))
             throw StatusError(VCSRMC_INVALID_ARG, "rows_unit_nnz must be 0 or a power of two in [16, 1024]");
@@ -437,7 +502,7 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
                 d->has_segment = true;
             }
             dev::RowViewHost rv;
-            if (plans & ((1 << VCSRMC_PLAN_ROWS) | (1 << VCSRMC_PLAN_BAND))) {
+            if (plans & ((1 << VCSRMC_PLAN_ROWS) | (1 << VCSRMC_PLAN_BAND) | (1 << VCSRMC_PLAN_HYBRID))) {
                 if (unit_nnz == 0) {
                     int sms = 0;
                     cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
@@ -448,10 +513,13 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
                 // The default layouts add the BAND plan (FP16 format) where it beats ROWS:
                 // enough entries per tensor-core tile.
                 dev::BandChoice bc{dev::kBandRows, 0.0};
-                if ((plans & (1 << VCSRMC_PLAN_BAND)) || (default_plans && !v.fp32)) bc = dev::choose_band(rv, v.M);
+                if ((plans & ((1 << VCSRMC_PLAN_BAND) | (1 << VCSRMC_PLAN_HYBRID))) || (default_plans && !v.fp32))
+                    bc = dev::choose_band(rv, v.M);
                 if (opts->band_rows > 0) bc.band_rows = opts->band_rows;
                 if (default_plans && !v.fp32 && bc.entries_per_tile >= dev::kBandMinEntriesPerTile)
                     plans |= 1 << VCSRMC_PLAN_BAND;
+                else if (default_plans && !v.fp32 && bc.dense_fraction >= dev::kHybridMinDenseFraction)
+                    plans |= 1 << VCSRMC_PLAN_HYBRID;
                 if (plans & (1 << VCSRMC_PLAN_BAND)) {
                     dev::BandViewHost bv = dev::build_band_view(rv, v.M, bc.band_rows, nth);
                     d->band_rows = bv.band_rows;
@@ -463,6 +531,34 @@ VCSRMC_EXPORT int vcsrmc_upload_opts(const vcsrmc_format* f, int device, const v
                     d->ents = upload_array(bv.ents.data(), bv.ents.size(), st);
                     cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
                     d->has_band = true;
+                }
+                if (plans & (1 << VCSRMC_PLAN_HYBRID)) {
+                    const dev::BandViewHost full = dev::build_band_view(rv, v.M, bc.band_rows, nth);
+                    dev::RowViewHost dense, resid;
+                    dev::split_dense_tiles(rv, full, v.M, int(dev::kBandMinEntriesPerTile), nth, dense, resid);
+                    const dev::BandViewHost bv = dev::build_band_view(dense, v.M, bc.band_rows, nth);
+                    // the rows part runs in accumulate mode only: units over non-empty rows
+                    dev::pack_units(resid.rp.data(), v.M, unit_nnz, resid.units, resid.split_rows, true);
+                    d->hb_rows = bv.band_rows;
+                    d->hb_bands = int(bv.tile_ptr.size()) - 1;
+                    d->hb_tiles = int64_t(bv.tile_col.size());
+                    d->hb_nnz = int64_t(bv.ents.size());
+                    d->hb_tile_ptr = upload_array(bv.tile_ptr.data(), bv.tile_ptr.size(), st);
+                    d->hb_tile_col = upload_array(bv.tile_col.data(), bv.tile_col.size(), st);
+                    d->hb_tile_eptr = upload_array(bv.tile_eptr.data(), bv.tile_eptr.size(), st);
+                    d->hb_ents = upload_array(bv.ents.data(), bv.ents.size(), st);
+                    d->hr_nnz = int64_t(resid.cols.size());
+                    d->hr_rp = upload_array(resid.rp.data(), resid.rp.size(), st);
+                    d->hr_cols = upload_array(resid.cols.data(), resid.cols.size(), st);
+                    std::vector<__half> h(resid.vals.size());
+                    for (size_t i = 0; i < h.size(); ++i) h[i] = __float2half_rn(resid.vals[i]);
+                    d->hr_vals = upload_array(h.data(), h.size(), st);
+                    d->hr_units = reinterpret_cast<int4*>(upload_array(resid.units.data(), resid.units.size(), st));
+                    d->hr_n_units = int64_t(resid.units.size());
+                    d->hr_split = upload_array(resid.split_rows.data(), resid.split_rows.size(), st);
+                    d->hr_n_split = int(resid.split_rows.size());
+                    cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+                    d->has_hybrid = true;
                 }
             }
             if (plans & (1 << VCSRMC_PLAN_ROWS)) {
@@ -524,7 +620,11 @@ VCSRMC_EXPORT int vcsrmc_device_info_get(const vcsrmc_device_format* d, vcsrmc_d
         i.fp32 = d->fp32;
         i.scale = d->scale;
         i.plans = (d->has_segment ? 1 << VCSRMC_PLAN_SEGMENT : 0) | (d->has_rows ? 1 << VCSRMC_PLAN_ROWS : 0) |
-                  (d->has_band ? 1 << VCSRMC_PLAN_BAND : 0);
+                  (d->has_band ? 1 << VCSRMC_PLAN_BAND : 0) | (d->has_hybrid ? 1 << VCSRMC_PLAN_HYBRID : 0);
+        i.hybrid_band_rows = d->hb_rows;
+        i.hybrid_tiles = d->hb_tiles;
+        i.hybrid_band_nnz = d->hb_nnz;
+        i.hybrid_rows_nnz = d->hr_nnz;
         i.n_groups = d->n_groups;
         i.n_slots = d->n_slots;
         i.n_items = d->n_items;
@@ -645,6 +745,8 @@ VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const i
             throw StatusError(VCSRMC_INVALID_ARG, "unknown plan bits");
         if ((plans & (1 << VCSRMC_PLAN_BAND)) && fp32)
             throw StatusError(VCSRMC_INVALID_ARG, "the BAND plan runs on the tensor cores and needs the FP16 format");
+        if (plans & (1 << VCSRMC_PLAN_HYBRID))
+            throw StatusError(VCSRMC_INVALID_ARG, "the HYBRID layout is built at upload (vcsrmc_upload_ex), not here");
         int unit_nnz = o.rows_unit_nnz;
         if (unit_nnz != 0 && (unit_nnz < 16 || unit_nnz > dev::kUnitNnzMax || (unit_nnz & (unit_nnz - 1))))
             throw StatusError(VCSRMC_INVALID_ARG, "rows_unit_nnz must be 0 or a power of two in [16, 1024]");

@@ -570,16 +570,21 @@ BandChoice choose_band_sampled(int M, const BandSampleFetch& fetch) {
     size_t i = 0;
     for (const int H : kCandidates) {
         const int samples = std::min((M + H - 1) / H, 64);
-        int64_t tiles = 0, rows = 0, ents = 0;
+        int64_t tiles = 0, rows = 0, ents = 0, dense = 0;
         for (int k = 0; k < samples; ++k, ++i) {
             cols.assign(first[i], last[i]);
             std::sort(cols.begin(), cols.end());
-            int64_t end = -1;  // greedy tiles, as build_band_view cuts them
-            for (const int c : cols)
+            int64_t end = -1, in_tile = 0;  // greedy tiles, as build_band_view cuts them
+            for (const int c : cols) {
                 if (c >= end) {
+                    if (in_tile >= int64_t(kBandMinEntriesPerTile)) dense += in_tile;
                     ++tiles;
                     end = int64_t(c) + kBandK;
+                    in_tile = 0;
                 }
+                ++in_tile;
+            }
+            if (in_tile >= int64_t(kBandMinEntriesPerTile)) dense += in_tile;
             rows += ranges[i].second - ranges[i].first;
             ents += int64_t(cols.size());
         }
@@ -587,7 +592,8 @@ BandChoice choose_band_sampled(int M, const BandSampleFetch& fetch) {
         const double cost = (double(tiles) + 2.0 * samples) / double(std::max<int64_t>(rows, 1));
         if (H == kCandidates[0] || cost < best_cost * 0.995) {
             best_cost = cost;
-            best = BandChoice{H, tiles > 0 ? double(ents) / double(tiles) : 0.0};
+            best = BandChoice{H, tiles > 0 ? double(ents) / double(tiles) : 0.0,
+                              ents > 0 ? double(dense) / double(ents) : 0.0};
         }
     }
     return best;
@@ -599,6 +605,59 @@ BandChoice choose_band(const RowViewHost& rv, int M) {
         for (size_t i = 0; i < ranges.size(); ++i) {
             first[i] = rv.cols.data() + rv.rp[size_t(ranges[i].first)];
             last[i] = rv.cols.data() + rv.rp[size_t(ranges[i].second)];
+        }
+    });
+}
+
+void split_dense_tiles(const RowViewHost& rv, const BandViewHost& bv, int M, int min_entries, int nthreads,
+                       RowViewHost& dense, RowViewHost& resid) {
+    const int H = bv.band_rows;
+    const int nb = int(bv.tile_ptr.size()) - 1;
+    const int64_t nnz = M > 0 ? rv.rp[M] : 0;
+    if (nb != (M + H - 1) / H) throw StatusError(VCSRMC_INTERNAL, "band view does not match the row view");
+    std::vector<uint8_t> in_dense(size_t(std::max<int64_t>(nnz, 1)), 0);
+    dense.rp.assign(size_t(M) + 1, 0);
+    resid.rp.assign(size_t(M) + 1, 0);
+    const int nth = resolve_threads(nthreads);
+    parallel_for_dynamic(0, nb, nth, 64, [&](int64_t lo, int64_t hi) {
+        for (int64_t b = lo; b < hi; ++b) {
+            const int t0 = bv.tile_ptr[size_t(b)], t1 = bv.tile_ptr[size_t(b) + 1];
+            for (int r = int(b) * H; r < std::min(M, int(b + 1) * H); ++r) {
+                int t = t0, nd = 0;
+                for (int p = rv.rp[r]; p < rv.rp[r + 1]; ++p) {  // columns ascend, and so do the tiles
+                    const int c = rv.cols[size_t(p)];
+                    while (t + 1 < t1 && bv.tile_col[size_t(t) + 1] <= c) ++t;
+                    if (t >= t1 || c < bv.tile_col[size_t(t)] || c >= bv.tile_col[size_t(t)] + kBandK)
+                        throw StatusError(VCSRMC_INTERNAL, "entry outside its band's tiles");
+                    const bool d = bv.tile_eptr[size_t(t) + 1] - bv.tile_eptr[size_t(t)] >= min_entries;
+                    in_dense[size_t(p)] = d ? 1 : 0;
+                    nd += d ? 1 : 0;
+                }
+                dense.rp[size_t(r) + 1] = nd;
+                resid.rp[size_t(r) + 1] = (rv.rp[r + 1] - rv.rp[r]) - nd;
+            }
+        }
+    });
+    for (int r = 0; r < M; ++r) {
+        dense.rp[size_t(r) + 1] += dense.rp[size_t(r)];
+        resid.rp[size_t(r) + 1] += resid.rp[size_t(r)];
+    }
+    dense.cols.resize(size_t(dense.rp[size_t(M)]));
+    dense.vals.resize(dense.cols.size());
+    resid.cols.resize(size_t(resid.rp[size_t(M)]));
+    resid.vals.resize(resid.cols.size());
+    parallel_for(0, M, nth, [&](int64_t lo, int64_t hi) {
+        for (int64_t r = lo; r < hi; ++r) {
+            int qd = dense.rp[size_t(r)], qr = resid.rp[size_t(r)];
+            for (int p = rv.rp[r]; p < rv.rp[r + 1]; ++p) {
+                if (in_dense[size_t(p)]) {
+                    dense.cols[size_t(qd)] = rv.cols[size_t(p)];
+                    dense.vals[size_t(qd++)] = rv.vals[size_t(p)];
+                } else {
+                    resid.cols[size_t(qr)] = rv.cols[size_t(p)];
+                    resid.vals[size_t(qr++)] = rv.vals[size_t(p)];
+                }
+            }
         }
     });
 }

@@ -38,11 +38,16 @@ struct BandViewHost {
 };
 
 // The band height (<= 128) that minimises tiles per row (plus a per-band cost), estimated on a
-// sample of bands, and the mean entries per tile it gives.
+// sample of bands, the mean entries per tile it gives, and the fraction of the sampled entries in
+// tiles holding at least kBandMinEntriesPerTile entries (the HYBRID plan's dense part).
 struct BandChoice {
     int band_rows;
     double entries_per_tile;
+    double dense_fraction = 0.0;
 };
+// The default layouts add HYBRID (FP16 format, upload only) where BAND alone does not pay but at
+// least this fraction of the entries sits in dense tiles.
+constexpr double kHybridMinDenseFraction = 0.5;
 BandChoice choose_band(const RowViewHost& rv, int M);
 
 // The same choice from any source of the sampled bands: fetch(ranges, first, last) makes
@@ -55,6 +60,14 @@ BandChoice choose_band_sampled(int M, const BandSampleFetch& fetch);
 // From the row view (rows' entries in ascending column order, values already divided by the
 // format's scale). nthreads <= 0: all host threads.
 BandViewHost build_band_view(const RowViewHost& rv, int M, int band_rows, int nthreads);
+
+// Hybrid plan: tiles of the band view `bv` (built from `rv` at its band height) that hold at least
+// min_entries entries are "dense". Their entries go to `dense`, all others to `resid`; both row
+// views keep every row's ascending column order and values, and the band view of `dense` at the
+// same height has exactly the dense tiles (a dense tile starts at its first entry's column, which
+// stays the first uncovered column once the sparse tiles are gone). Units are not packed.
+void split_dense_tiles(const RowViewHost& rv, const BandViewHost& bv, int M, int min_entries, int nthreads,
+                       RowViewHost& dense, RowViewHost& resid);
 
 struct BandPlanView {
     const int* tile_ptr;

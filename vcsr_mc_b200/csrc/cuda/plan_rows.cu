@@ -605,7 +605,7 @@ int choose_unit_nnz(int64_t nnz, int sms) {
 }
 
 void pack_units(const int* rp, int M, int unit_nnz, std::vector<RowViewHost::Unit>& units,
-                std::vector<int>& split_rows) {
+                std::vector<int>& split_rows, bool skip_empty) {
     units.clear();
     split_rows.clear();
     // heavy-row chunks first, then runs of light rows
@@ -619,7 +619,7 @@ void pack_units(const int* rp, int M, int unit_nnz, std::vector<RowViewHost::Uni
     }
     int r = 0;
     while (r < M) {
-        if (rp[r + 1] - rp[r] > unit_nnz) { ++r; continue; }
+        if (rp[r + 1] - rp[r] > unit_nnz || (skip_empty && rp[r + 1] == rp[r])) { ++r; continue; }
         const int rb = r;
         int n = 0;
         while (r < M && r - rb < kUnitRows) {

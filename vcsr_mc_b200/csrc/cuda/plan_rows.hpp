@@ -27,9 +27,11 @@ struct RowViewHost {
 RowViewHost build_row_view(const VCSRMC& v, int unit_nnz);
 // The work units of a row view from its row_ptr alone: every row with more than unit_nnz entries
 // as unit_nnz-entry chunks (listed first, and in split_rows), then greedy runs of at most
-// kUnitRows consecutive lighter rows with together at most unit_nnz entries.
+// kUnitRows consecutive lighter rows with together at most unit_nnz entries. With skip_empty, no
+// run starts at an empty row (for a view run in accumulate mode only, where empty rows need no
+// store; a run may still hold empty rows between non-empty ones).
 void pack_units(const int* rp, int M, int unit_nnz, std::vector<RowViewHost::Unit>& units,
-                std::vector<int>& split_rows);
+                std::vector<int>& split_rows, bool skip_empty = false);
 // The unit size for a matrix of `nnz` entries on a GPU with `sms` SMs: the largest power of two
 // in [16, 256] that still gives every resident lane group (48 per SM) about four units.
 int choose_unit_nnz(int64_t nnz, int sms);

@@ -178,6 +178,61 @@ CSR gen_stencil27(int nx, int ny, int nz, uint64_t seed, int nthreads) {
     return csr;
 }
 
+CSR gen_stencil27_links(int n, int links, uint64_t seed, int nthreads) {
+    if (links < 0 || links > 64) throw std::runtime_error("links per row out of range");
+    const CSR st = gen_stencil27(n, n, n, seed, nthreads);
+    nthreads = resolve_threads(nthreads);
+    const int M = st.M;
+    const uint64_t kl = vrng_key(seed, VRNG_STREAM_LINKS);
+    // row i's extra columns, in draw order, without stencil columns or repeats
+    auto extra = [&](int64_t i, std::vector<std::pair<int, float>>& out) {
+        out.clear();
+        const int* b = st.col.data() + st.row_ptr[i];
+        const int* e = st.col.data() + st.row_ptr[i + 1];
+        for (int t = 0; t < links; ++t) {
+            const uint64_t d = 2 * (uint64_t(i) * uint64_t(links) + uint64_t(t));
+            const int c = int(vrng_at(kl, d) % uint64_t(M));
+            if (std::binary_search(b, e, c)) continue;
+            bool seen = false;
+            for (const auto& x : out) seen = seen || x.first == c;
+            if (!seen) out.push_back({c, float(vrng_sym(vrng_at(kl, d + 1)))});
+        }
+    };
+    CSR csr;
+    csr.M = csr.N = M;
+    csr.row_ptr.assign(size_t(M) + 1, 0);
+    parallel_for(0, M, nthreads, [&](int64_t lo, int64_t hi) {
+        std::vector<std::pair<int, float>> x;
+        for (int64_t i = lo; i < hi; ++i) {
+            extra(i, x);
+            csr.row_ptr[size_t(i) + 1] = (st.row_ptr[i + 1] - st.row_ptr[i]) + int(x.size());
+        }
+    });
+    int64_t total = 0;
+    for (int r = 0; r < M; ++r) {
+        total += csr.row_ptr[size_t(r) + 1];
+        if (total > INT_MAX) throw std::runtime_error("generated nnz exceeds 32-bit limit");
+        csr.row_ptr[size_t(r) + 1] = int(total);
+    }
+    csr.nnz = int(total);
+    csr.col.resize(size_t(total));
+    csr.val.resize(size_t(total));
+    parallel_for(0, M, nthreads, [&](int64_t lo, int64_t hi) {
+        std::vector<std::pair<int, float>> x;
+        for (int64_t i = lo; i < hi; ++i) {
+            extra(i, x);
+            for (int p = st.row_ptr[i]; p < st.row_ptr[i + 1]; ++p) x.push_back({st.col[size_t(p)], st.val[size_t(p)]});
+            std::sort(x.begin(), x.end(), [](const auto& u, const auto& v) { return u.first < v.first; });
+            int q = csr.row_ptr[size_t(i)];
+            for (const auto& e : x) {
+                csr.col[size_t(q)] = e.first;
+                csr.val[size_t(q++)] = e.second;
+            }
+        }
+    });
+    return csr;
+}
+
 CSR gen_rmat(int scale, int64_t edges, double a, double b, double c, uint64_t seed, int nthreads) {
     if (scale < 1 || scale > 30 || edges < 0 || a < 0 || b < 0 || c < 0 || a + b + c > 1)
         throw std::runtime_error("bad R-MAT parameters");

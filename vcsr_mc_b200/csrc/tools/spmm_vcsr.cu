@@ -2,8 +2,12 @@
 //   --mtx FILE | --gen c1|c2|c3|rmat[:scale]  --O 128 --segw 16 --tileK 64 --repeat 10 --warmup 3
 //   --stat mean|median --reorder none|rcm --algo vcsr_mc,vcsr_mc_fp32,cusparse,cusparse_fp16|all
 //   --check cpu|none --csv --bdist pattern|normal|uniform|wide --lenient
-// plus: --gen (seeded synthetic configurations, no download needed), --seed, --plan auto|rows|segment|band,
-// --b16 (the FP16 path reads fp16 B instead of converting fp32 B).
+// plus: --gen (seeded synthetic configurations, no download needed), --seed, --plan auto|rows|segment|band|hybrid,
+// --b16 (the FP16 path reads fp16 B instead of converting fp32 B), --flush-l2 (write a buffer twice
+// the L2 size before every launch, outside the timed events), --peak-gbs G (the HBM peak that
+// roofline_frac is taken against). Two columns follow the reference's CSV columns and `plan`:
+// gbps_alg (algorithmic bytes per second: A's column index and value, row_ptr, the B rows A
+// touches, C written once) and roofline_frac (gbps_alg / peak, empty without --peak-gbs).
 // Same B fill (fixed seed 20260923), same fp64 CPU check and acceptance bounds, same CSV schema.
 // Host work uses the library's C++ surface (vcsrmc/*.hpp); every GPU call goes through the C ABI
 // (vcsrmc.h). "vcsr_mc"/"vcsr_mc_fp32" with --plan auto and fp32 B run exactly like the reference
@@ -55,12 +59,12 @@ void abi_ok(int st) {
 
 void usage() {
     std::printf(
-        "Usage: spmm_vcsr (--mtx file.mtx | --gen c1|c2|c3|rmat[:scale]) --O 128 [options]\n"
+        "Usage: spmm_vcsr (--mtx file.mtx | --gen c1|c2|c3|c3links|rmat[:scale]) --O 128 [options]\n"
         "Algorithms: vcsr_mc (FP16 A/B, FP32 accumulate), vcsr_mc_fp32, cusparse (FP32),\n"
         "            cusparse_fp16 (FP16 A and B, FP32 compute and C), all\n"
         "Options: --segw 16 --tileK 64 --repeat 10 --warmup 3 --stat mean|median\n"
         "         --reorder none|rcm --check cpu|none --csv --bdist pattern|normal|uniform|wide\n"
-        "         --lenient --seed 0 --plan auto|rows|segment|band --b16\n"
+        "         --lenient --seed 0 --plan auto|rows|segment|band|hybrid --b16 --flush-l2 --peak-gbs G\n"
         "tileK must be one of 16, 32, 64, 128, 256; segw one of 16, 32, 48, 64.\n");
 }
 
@@ -85,11 +89,12 @@ CSR generate(const std::string& spec, uint64_t seed) {
     if (spec == "c1") return gen_uniform_poisson(4096, 4096, 16.0, seed);
     if (spec == "c2") return gen_zipf_rows(262144, 262144, 1.8, 8192, 10.0, seed);
     if (spec == "c3") return gen_stencil27(100, 100, 100, seed);
+    if (spec == "c3links") return gen_stencil27_links(100, 3, seed);
     if (spec.rfind("rmat", 0) == 0) {
         const int scale = spec.size() > 5 ? int_at_least(spec.c_str() + 5, 1) : 24;
         return gen_rmat(scale, int64_t(1) << (scale + 4), 0.57, 0.19, 0.19, seed);
     }
-    throw std::runtime_error("Unknown --gen: " + spec + " (c1|c2|c3|rmat[:scale])");
+    throw std::runtime_error("Unknown --gen: " + spec + " (c1|c2|c3|c3links|rmat[:scale])");
 }
 
 // fp64 CSR SpMM, row blocks on all host threads; per-row accumulation order of the reference.
@@ -180,6 +185,7 @@ struct ResultRow {
     std::string algo, validation, plan;
     double ms = 0, gflops = 0, rel_l2 = 0, ms_mean = 0, ms_median = 0;
     double setup_ms = 0, convert_ms = 0, upload_ms = 0;
+    double gbps_alg = 0, roofline_frac = -1;  // frac < 0: no peak given
 };
 // Fixed columns of every row of a run.
 struct RunColumns {
@@ -188,19 +194,28 @@ struct RunColumns {
 };
 constexpr const char* kCsvHeader =
     "gpu,sm,mtx,O,segw,bundle,tileK,repeat,algo,ms,gflops,validation,rel_l2,setup_ms,ms_mean,ms_median,"
-    "convert_ms,upload_ms,plan";
+    "convert_ms,upload_ms,plan,gbps_alg,roofline_frac";
 
 void print_result(const ResultRow& r, const RunColumns& run, bool csv) {
     if (csv) {
-        std::printf("%s,%d,%s,%d,%d,%d,%d,%d,%s,%.9g,%.9g,%s,%.9g,%.6g,%.9g,%.9g,%.6g,%.6g,%s\n",
+        char frac[32] = "";
+        if (r.roofline_frac >= 0) std::snprintf(frac, sizeof frac, "%.6g", r.roofline_frac);
+        std::printf("%s,%d,%s,%d,%d,%d,%d,%d,%s,%.9g,%.9g,%s,%.9g,%.6g,%.9g,%.9g,%.6g,%.6g,%s,%.6g,%s\n",
                     csv_quote(run.gpu).c_str(), run.sm, csv_quote(run.source).c_str(), run.O, run.segw, run.bundle,
                     run.tileK, run.repeat, r.algo.c_str(), r.ms, r.gflops, r.validation.c_str(), r.rel_l2,
-                    r.setup_ms, r.ms_mean, r.ms_median, r.convert_ms, r.upload_ms, r.plan.c_str());
+                    r.setup_ms, r.ms_mean, r.ms_median, r.convert_ms, r.upload_ms, r.plan.c_str(), r.gbps_alg, frac);
     } else {
         std::printf("%-20s %10.6f %12.2f   %s (rel_l2=%.3g, setup %.3f ms, plan %s)\n", r.algo.c_str(), r.ms,
                     r.gflops, r.validation.c_str(), r.rel_l2, r.setup_ms, r.plan.c_str());
     }
     std::fflush(stdout);
+}
+
+// Compulsory bytes of one SpMM: per entry its column index and value (a_bytes), row_ptr, the
+// `distinct` rows of B that A touches (O values of b_bytes each), and C (fp32) written once.
+double algorithmic_bytes(const CSR& csr, int64_t distinct, int O, int a_bytes, int b_bytes) {
+    return double(csr.nnz) * (4 + a_bytes) + (double(csr.M) + 1) * 4 + double(distinct) * O * b_bytes +
+           double(csr.M) * O * 4;
 }
 
 // Host wall time of one call, in milliseconds.
@@ -220,7 +235,8 @@ static int benchmark_main(int argc, char** argv) {
                          plan = "auto";
     int O = 128, segw = 16, tileK = 64, repeat = 10, warmup = 3;
     uint64_t seed = 0;
-    bool csv = false, lenient = false, b16 = false;
+    bool csv = false, lenient = false, b16 = false, flush_l2 = false;
+    double peak_gbs = 0;
     constexpr int bundle = 16;
     static option opts[] = {
         {"mtx", required_argument, nullptr, 'm'},    {"gen", required_argument, nullptr, 'g'},
@@ -232,6 +248,7 @@ static int benchmark_main(int argc, char** argv) {
         {"bdist", required_argument, nullptr, 'D'},  {"lenient", no_argument, nullptr, 'L'},
         {"stat", required_argument, nullptr, 'S'},   {"seed", required_argument, nullptr, 'e'},
         {"plan", required_argument, nullptr, 'p'},   {"b16", no_argument, nullptr, 'b'},
+        {"flush-l2", no_argument, nullptr, 'F'},     {"peak-gbs", required_argument, nullptr, 'P'},
         {nullptr, 0, nullptr, 0}};
     int opt;
     while ((opt = getopt_long(argc, argv, "", opts, nullptr)) != -1) {
@@ -252,6 +269,8 @@ static int benchmark_main(int argc, char** argv) {
             case 'e': seed = std::strtoull(optarg, nullptr, 10); break;
             case 'p': plan = optarg; break;
             case 'b': b16 = true; break;
+            case 'F': flush_l2 = true; break;
+            case 'P': peak_gbs = std::strtod(optarg, nullptr); break;
             case 'j': csv = true; break;
             case 'h': usage(); return 0;
             default: usage(); return 2;
@@ -276,11 +295,12 @@ static int benchmark_main(int argc, char** argv) {
     if ((mtx.empty() == gen.empty()) || optind != argc) { usage(); return 2; }
     if (reorder != "none" && reorder != "rcm") throw std::runtime_error("Unknown reordering: " + reorder);
     if (stat != "mean" && stat != "median") throw std::runtime_error("Unknown --stat: " + stat + " (mean|median)");
-    if (plan != "auto" && plan != "rows" && plan != "segment" && plan != "band")
+    if (plan != "auto" && plan != "rows" && plan != "segment" && plan != "band" && plan != "hybrid")
         throw std::runtime_error("Unknown --plan: " + plan);
     const int plan_id = plan == "rows"      ? VCSRMC_PLAN_ROWS
                         : plan == "segment" ? VCSRMC_PLAN_SEGMENT
                         : plan == "band"    ? VCSRMC_PLAN_BAND
+                        : plan == "hybrid"  ? VCSRMC_PLAN_HYBRID
                                             : VCSRMC_PLAN_AUTO;
 
     CSR csr = mtx.empty() ? generate(gen, seed) : coo_to_csr(read_matrix_market_coo(mtx));
@@ -322,6 +342,19 @@ static int benchmark_main(int argc, char** argv) {
 
     std::vector<double> reference;
     if (check == "cpu") reference = cpu_reference(csr, hB, O);
+    int64_t distinct = 0;
+    {
+        std::vector<char> used(size_t(std::max(csr.N, 1)), 0);
+        for (int p = 0; p < csr.nnz; ++p) used[size_t(csr.col[p])] = 1;
+        for (char u : used) distinct += u;
+    }
+    void* flush_buf = nullptr;
+    size_t flush_bytes = 0;
+    if (flush_l2) {
+        flush_bytes = 2 * size_t(std::max(device.l2CacheSize, 1 << 20));
+        cuda_ok(cudaMalloc(&flush_buf, flush_bytes), "cudaMalloc");
+    }
+    int flushes = 0;
     RunColumns run_cols;
     run_cols.gpu = device.name;
     run_cols.sm = device.major * 10 + device.minor;
@@ -342,6 +375,7 @@ static int benchmark_main(int argc, char** argv) {
     // One launch on a zeroed C (C += A*B), its event time in ms.
     auto launch_once = [&](const std::function<float()>& run) {
         cuda_ok(cudaMemsetAsync(dC, 0, elementsC * sizeof(float), st), "cudaMemsetAsync");
+        if (flush_buf) cuda_ok(cudaMemsetAsync(flush_buf, ++flushes & 0xff, flush_bytes, st), "cudaMemsetAsync");
         cuda_ok(cudaStreamSynchronize(st), "cudaStreamSynchronize");
         const float ms = csr.nnz ? run() : 0.f;
         cuda_ok(cudaStreamSynchronize(st), "cudaStreamSynchronize");
@@ -376,6 +410,14 @@ static int benchmark_main(int argc, char** argv) {
         row.ms_median = t.median;
         row.ms = stat == "median" ? t.median : t.mean;
         row.gflops = row.ms > 0 ? (2.0 * csr.nnz * O) / (row.ms * 1e6) : 0;
+        {
+            const std::string k(name);
+            const bool fp16_a = k == "vcsr_mc" || k == "cusparse_fp16";
+            const bool fp16_b = k == "cusparse_fp16" || (k == "vcsr_mc" && b16);
+            const double bytes = algorithmic_bytes(csr, distinct, O, fp16_a ? 2 : 4, fp16_b ? 2 : 4);
+            row.gbps_alg = row.ms > 0 ? bytes / (row.ms * 1e6) : 0;
+            if (peak_gbs > 0) row.roofline_frac = row.gbps_alg / peak_gbs;
+        }
         row.setup_ms = setup_ms;
         row.convert_ms = convert_ms;
         row.upload_ms = upload_ms;
@@ -406,9 +448,10 @@ static int benchmark_main(int argc, char** argv) {
             vcsrmc_device_format* hd = nullptr;
             abi_ok(vcsrmc_csr_from_arrays(csr.M, csr.N, csr.nnz, csr.row_ptr.data(), csr.col.data(), csr.val.data(), &hc));
             abi_ok(vcsrmc_build_host(hc, fp32 ? 1 : 0, segw, 0, &hf));
-            // the BAND plan runs on the tensor cores (FP16 format); the FP32 format takes ROWS
-            const int my_plan = (plan_id == VCSRMC_PLAN_BAND && fp32) ? VCSRMC_PLAN_ROWS : plan_id;
-            const int mask = my_plan == VCSRMC_PLAN_BAND ? (1 << VCSRMC_PLAN_BAND) : 0;
+            // the BAND and HYBRID plans run on the tensor cores (FP16 format); the FP32 format takes ROWS
+            const bool tensor_plan = plan_id == VCSRMC_PLAN_BAND || plan_id == VCSRMC_PLAN_HYBRID;
+            const int my_plan = (tensor_plan && fp32) ? VCSRMC_PLAN_ROWS : plan_id;
+            const int mask = (my_plan == VCSRMC_PLAN_BAND || my_plan == VCSRMC_PLAN_HYBRID) ? (1 << my_plan) : 0;
             const char* my_plan_name = my_plan == plan_id ? plan.c_str() : "rows";
             const float upload = host_ms([&] { abi_ok(vcsrmc_upload_ex(hf, device_id, mask, st, &hd)); });
             measure(name,
@@ -469,6 +512,7 @@ static int benchmark_main(int argc, char** argv) {
         }, 0.f, 0.f, 0.f, "-");
     }
     cudaStreamDestroy(st);
+    cudaFree(flush_buf);
     cudaFree(dB); cudaFree(dC); cudaFree(dB16); cudaFree(d_val16);
     cudaFree(d_rowptr); cudaFree(d_col); cudaFree(d_val);
     return 0;

@@ -8,7 +8,7 @@ from __future__ import annotations
 import numpy as np
 
 GAMMA = np.uint64(0x9E3779B97F4A7C15)
-STREAM_ROWLEN, STREAM_COLS, STREAM_VALS, STREAM_DENSE, STREAM_RMAT = 1, 2, 3, 4, 5
+STREAM_ROWLEN, STREAM_COLS, STREAM_VALS, STREAM_DENSE, STREAM_RMAT, STREAM_LINKS = 1, 2, 3, 4, 5, 6
 
 
 def mix64(z):
