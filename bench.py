@@ -390,7 +390,9 @@ def main() -> None:
     config = {"workload": spec["desc"], "O": O_COLS, "segw": args.segw, "tileK": args.tileK,
               "path": (("fp16 A/B, fp32 accumulate, " if fp16 else "fp32, ") +
                        ("CUDA-core FFMA" if (args.plan == "rows" or not fp16) else "tcgen05 MMA, TMEM accumulator")),
-              "plan": {"rows": "rows: row-stationary over the VCSR-MC row view, C stored once",
+              "plan": {"rows": "rows: row-stationary over the VCSR-MC row view (for a GPU-built format the row view "
+                               "is the CSR itself with fp16 values, so this is a CSR SpMM; the VCSR-MC arrays feed the "
+                               "SEGMENT/BAND plans and validation), C stored once",
                        "segment": "segment: reference dataflow, per-item B segment, C reductions",
                        "band": "band: 128-row bands x {band_cols}-column tiles on tcgen05, TMEM accumulator, C stored once",
                        "hybrid": "hybrid: band tiles with >= 64 entries on tcgen05 (C stored once), the other entries "
@@ -450,8 +452,6 @@ def main() -> None:
                                np.asarray(col[p0:p1]), np.asarray(val[p0:p1]))
     nthreads = max(1, cores // world)
     plan = {"rows": vm.PLAN_ROWS, "segment": vm.PLAN_SEGMENT, "band": vm.PLAN_BAND, "hybrid": vm.PLAN_HYBRID}[args.plan]
-    if plan == vm.PLAN_HYBRID and args.build == "device":
-        args.build = "host"  # the hybrid layout is made by an upload
     hot = {"hot_rows": args.hot_rows, "hot_budget_mib": args.hot_budget_mib, "hot_persist": args.hot_persist,
            "hot_evict_first": args.hot_evict_first}
     torch.cuda.synchronize()

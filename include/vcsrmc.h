@@ -52,7 +52,7 @@ extern "C" {
  *          few column windows (stencils, banded or reordered matrices).
  * HYBRID:  FP16 format only: the band tiles that hold at least 64 entries run as BAND (C written
  *          once), every other entry then runs on ROWS, added into C. For matrices with dense
- *          blocks and scattered entries. Built by an upload (vcsrmc_upload_ex), not on the GPU.
+ *          blocks and scattered entries.
  * AUTO:    the first resident layout of BAND (fp16 B only), HYBRID (fp16 B only), ROWS,
  *          SEGMENT, BAND, HYBRID.                                                           */
 #define VCSRMC_PLAN_AUTO 0

@@ -119,8 +119,8 @@ def test_hybrid_errors(cuda):
     assert e.value.status == 1
     rp, col, val = A.arrays()
     t = lambda a, dt: cuda.from_numpy(np.ascontiguousarray(a)).to(device="cuda", dtype=dt)
-    with pytest.raises(vm.VcsrmcError) as e:  # built by an upload only
-        vm.build_vcsr_mc_device(t(rp, cuda.int32), t(col, cuda.int32), t(val, cuda.float32), A.M, A.N,
+    with pytest.raises(vm.VcsrmcError) as e:  # FP32 format on the GPU builder too
+        vm.build_vcsr_mc_device(t(rp, cuda.int32), t(col, cuda.int32), t(val, cuda.float32), A.M, A.N, fp32=True,
                                 plans=[vm.PLAN_HYBRID])
     assert e.value.status == 1
     dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=False, segw=32), device=0, plans=[vm.PLAN_ROWS])
@@ -133,13 +133,19 @@ def test_hybrid_errors(cuda):
 
 
 def test_default_layouts(cuda):
-    """An upload without a plan mask adds BAND on the stencil, HYBRID on the stencil with random
-    links (most entries in dense tiles, the mean tile too sparse for BAND alone), neither on the
-    power-law matrix; AUTO then runs that plan."""
+    """An upload (or a GPU build) without a plan mask adds BAND on the stencil, HYBRID on the stencil
+    with random links (most entries in dense tiles, the mean tile too sparse for BAND alone), neither
+    on the power-law matrix; AUTO then runs that plan."""
     want = {"c3": vm.PLAN_BAND, "mixed": vm.PLAN_HYBRID, "c2": None}
-    for name, plan in want.items():
+    for (name, plan), builder in [(x, b) for x in want.items() for b in ("upload", "device")]:
         A = matrix(name)
-        dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=False, segw=32), device=0)
+        if builder == "upload":
+            dV = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=False, segw=32), device=0)
+        else:
+            rp, col, val = A.arrays()
+            t = lambda a, dt: cuda.from_numpy(np.ascontiguousarray(a)).to(device="cuda", dtype=dt)
+            dV = vm.build_vcsr_mc_device(t(rp, cuda.int32), t(col, cuda.int32), t(val, cuda.float32), A.M, A.N,
+                                         fp32=False, segw=32)
         plans = dV.info()["plans"]
         tensor = [p for p in plans if p in (vm.PLAN_BAND, vm.PLAN_HYBRID)]
         assert tensor == ([] if plan is None else [plan]), (name, plans)
@@ -151,3 +157,54 @@ def test_default_layouts(cuda):
         ref, ab = ob.spmm_fp64(rp, col, val, B.float().cpu().numpy(), with_abs=True)
         check_fp16(C.cpu().numpy(), ref, ab)
         dV.free()
+
+
+@pytest.mark.parametrize("shape", ["empty-rows", "one-row", "narrow-N", "tiny"])
+def test_hybrid_edge_shapes(cuda, shape):
+    """Matrices with empty rows (whole empty bands), a single row, fewer columns than a tile, and a
+    handful of entries: the band part may have no tile at all and the rows part no entry."""
+    from tests.helpers import random_csr
+    M, N, d = {"empty-rows": (700, 900, 0.05), "one-row": (1, 300, 0.5), "narrow-N": (500, 20, 0.5),
+               "tiny": (5, 7, 0.3)}[shape]
+    rp, col, val = random_csr(M, N, d, seed=11, empty_rows=shape == "empty-rows")
+    if shape == "empty-rows":  # rows 200 .. 455 empty: two whole bands without entries
+        keep = np.repeat(np.arange(M), np.diff(rp))
+        mask = (keep < 200) | (keep >= 456)
+        counts = np.bincount(keep[mask], minlength=M)
+        rp = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+        col, val = col[mask], val[mask]
+    A = vm.CSR.from_arrays(M, N, rp, col, val)
+    C, Bu, info = run_hybrid(cuda, A, 40, True)
+    assert info["hybrid_band_nnz"] + info["hybrid_rows_nnz"] == A.nnz
+    ref, ab = ob.spmm_fp64(rp, col, val, Bu, with_abs=True)
+    check_fp16(C, ref, ab)
+
+
+@pytest.mark.parametrize("name", ["mixed", "c3", "rmat14", "c2"])
+def test_device_built_hybrid_equals_upload(cuda, name):
+    """The GPU builder's HYBRID layout is the upload's: the same band height, dense tiles and entry
+    split, and the same C (bit for bit outside rows reduced atomically in chunks, which are within
+    fp32 rounding)."""
+    A = matrix(name)
+    rp, col, val = A.arrays()
+    t = lambda a, dt: cuda.from_numpy(np.ascontiguousarray(a)).to(device="cuda", dtype=dt)
+    dD = vm.build_vcsr_mc_device(t(rp, cuda.int32), t(col, cuda.int32), t(val, cuda.float32), A.M, A.N, fp32=False,
+                                 segw=32, plans=[vm.PLAN_HYBRID])
+    dH = vm.upload_vcsr_mc_device(vm.csr_to_vcsr_mc(A, fp32=False, segw=32), device=0, plans=[vm.PLAN_HYBRID])
+    iD, iH = dD.info(), dH.info()
+    for k in ("hybrid_band_rows", "hybrid_tiles", "hybrid_band_nnz", "hybrid_rows_nnz"):
+        assert iD[k] == iH[k], (k, iD[k], iH[k])
+    assert vm.PLAN_BAND not in iD["plans"] and vm.PLAN_HYBRID in iD["plans"]
+    B = cuda.from_numpy(vm.gen_dense_host(A.N, 128, seed=8)).cuda().half()
+    out = []
+    for dV in (dD, dH):
+        C = cuda.full((A.M, 128), 4.0, device="cuda")
+        vm.spmm(dV, B, C, accumulate=False, plan=vm.PLAN_HYBRID)
+        cuda.cuda.synchronize()
+        assert dV.status() == 0
+        out.append(C.cpu().numpy())
+        dV.free()
+    ref, ab = ob.spmm_fp64(rp, col, val, B.float().cpu().numpy(), with_abs=True)
+    check_fp16(out[0], ref, ab)
+    diff = np.abs(out[0].astype(np.float64) - out[1])
+    assert np.all(diff <= 1e-5 * ab + 1e-30)

@@ -711,6 +711,194 @@ BandLayout build_band_layout(const int* row_ptr, const int* col, const float* va
     return L;
 }
 
+// ---- HYBRID plan: dense band tiles and the residual row view ------------------------------------
+namespace {
+
+// Per tile: dense (>= min entries) or not; per entry: the same flag and its tile; per tile: its band.
+__global__ void hybrid_tile_kernel(const int* __restrict__ tile_ptr, const int* __restrict__ tile_eptr, int nb,
+                                   int min_entries, int* __restrict__ tile_dense, int* __restrict__ tile_band,
+                                   int* __restrict__ ent_dense, int* __restrict__ ent_tile) {
+    for (int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; b < nb; b += int64_t(gridDim.x) * blockDim.x) {
+        for (int t = tile_ptr[b]; t < tile_ptr[b + 1]; ++t) {
+            const int e0 = tile_eptr[t], e1 = tile_eptr[t + 1];
+            const int d = e1 - e0 >= min_entries ? 1 : 0;
+            tile_dense[t] = d;
+            tile_band[t] = int(b);
+            for (int e = e0; e < e1; ++e) {
+                ent_dense[e] = d;
+                ent_tile[e] = t;
+            }
+        }
+    }
+}
+
+// The dense layout: tile t -> tpos[t], entry e -> epos[e]; band b's tiles start at tpos[tile_ptr[b]].
+__global__ void hybrid_dense_kernel(const int* __restrict__ tile_ptr, const int* __restrict__ tile_col,
+                                    const int* __restrict__ tile_eptr, const int* __restrict__ tile_dense,
+                                    const int* __restrict__ tpos, const int* __restrict__ epos, int nb, int64_t T,
+                                    int* __restrict__ d_tile_ptr, int* __restrict__ d_tile_col,
+                                    int* __restrict__ d_tile_eptr) {
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i <= nb; i += stride)
+        d_tile_ptr[i] = tpos[tile_ptr[i]];
+    for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < T; t += stride)
+        if (tile_dense[t]) {
+            d_tile_col[tpos[t]] = tile_col[t];
+            d_tile_eptr[tpos[t]] = epos[tile_eptr[t]];
+        }
+}
+
+// Dense entries to their compacted place; the others as (row << 32 | column) keys with fp16 values.
+__global__ void hybrid_entries_kernel(const uint32_t* __restrict__ ents, const int* __restrict__ ent_dense,
+                                      const int* __restrict__ ent_tile, const int* __restrict__ epos,
+                                      const int* __restrict__ tile_band, const int* __restrict__ tile_col, int H,
+                                      int64_t nnz, uint32_t* __restrict__ d_ents, uint64_t* __restrict__ r_key,
+                                      unsigned short* __restrict__ r_val) {
+    for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < nnz; e += int64_t(gridDim.x) * blockDim.x) {
+        const uint32_t w = ents[e];
+        if (ent_dense[e]) {
+            d_ents[epos[e]] = w;
+        } else {
+            const int t = ent_tile[e];
+            const int64_t r = e - epos[e];  // residual entries before e
+            const int row = tile_band[t] * H + int((w >> kBandColBits) & 127u);
+            const int col = tile_col[t] + int(w & uint32_t(kBandK - 1));
+            r_key[r] = (uint64_t(uint32_t(row)) << 32) | uint32_t(col);
+            r_val[r] = static_cast<unsigned short>(w >> 16);
+        }
+    }
+}
+
+// Residual row view from its sorted keys: columns, and the count of each row.
+__global__ void hybrid_resid_kernel(const uint64_t* __restrict__ key, int64_t n, int* __restrict__ cols,
+                                    int* __restrict__ row_count) {
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const uint64_t k = key[i];
+        cols[i] = int(uint32_t(k));
+        atomicAdd(row_count + int(k >> 32), 1);
+    }
+}
+
+// The dense layout's own invariants: band tile ranges inside [0, T), entry ranges increasing from 0
+// to D, tiles of a band in ascending, non-overlapping column order.
+__global__ void validate_dense_band_kernel(const int* __restrict__ tile_ptr, const int* __restrict__ tile_col,
+                                           const int* __restrict__ tile_eptr, int nb, int64_t T, int64_t D, int* bad) {
+    for (int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; b < nb; b += int64_t(gridDim.x) * blockDim.x) {
+        const int t0 = tile_ptr[b], t1 = tile_ptr[b + 1];
+        if (t0 < 0 || t1 < t0 || t1 > T) {
+            atomicOr(bad, 1);
+            continue;
+        }
+        for (int t = t0; t < t1; ++t)
+            if (tile_eptr[t] < 0 || tile_eptr[t + 1] <= tile_eptr[t] || tile_eptr[t + 1] > D || tile_col[t] < 0 ||
+                (t > t0 && int64_t(tile_col[t]) < int64_t(tile_col[t - 1]) + kBandK))
+                atomicOr(bad, 2);
+    }
+}
+
+}  // namespace
+
+HybridLayout build_hybrid_layout(const BandLayout& full, int M, int N, int64_t nnz, int min_entries, int unit_nnz,
+                                 cudaStream_t st) {
+    const int nb = full.n_bands, H = full.band_rows;
+    const int64_t T = full.n_tiles;
+    Buf<int> tile_dense(size_t(T) + 1), tile_band(size_t(std::max<int64_t>(T, 1))), tpos(size_t(T) + 1);
+    Buf<int> ent_dense(size_t(nnz) + 1), ent_tile(size_t(std::max<int64_t>(nnz, 1))), epos(size_t(nnz) + 1);
+    check(cudaMemsetAsync(tile_dense.p, 0, sizeof(int) * (size_t(T) + 1), st), "cudaMemsetAsync");
+    check(cudaMemsetAsync(ent_dense.p, 0, sizeof(int) * (size_t(nnz) + 1), st), "cudaMemsetAsync");
+    if (nb > 0) {
+        hybrid_tile_kernel<<<blocks_for(nb), 256, 0, st>>>(full.tile_ptr, full.tile_eptr, nb, min_entries, tile_dense.p,
+                                                           tile_band.p, ent_dense.p, ent_tile.p);
+        check(cudaGetLastError(), "hybrid_tile_kernel");
+    }
+    exclusive_scan(tile_dense.p, tpos.p, T + 1, st);
+    exclusive_scan(ent_dense.p, epos.p, nnz + 1, st);
+    const int64_t TD = read_one(tpos.p + T, st), D = read_one(epos.p + nnz, st), R = nnz - D;
+    if (TD < 0 || TD > T || D < 0 || D > nnz) throw StatusError(VCSRMC_INTERNAL, "hybrid split is inconsistent");
+    HybridLayout out;
+    out.dense_nnz = D;
+    out.resid_nnz = R;
+    // dense part
+    Buf<int> d_tile_ptr(size_t(nb) + 1), d_tile_col(size_t(std::max<int64_t>(TD, 1))), d_tile_eptr(size_t(TD) + 1);
+    Buf<uint32_t> d_ents(size_t(std::max<int64_t>(D, 1)));
+    const int D32 = int(D);
+    check(cudaMemcpyAsync(d_tile_eptr.p + TD, &D32, sizeof(int), cudaMemcpyHostToDevice, st), "cudaMemcpyAsync");
+    hybrid_dense_kernel<<<blocks_for(std::max<int64_t>(T, int64_t(nb) + 1)), 256, 0, st>>>(
+        full.tile_ptr, full.tile_col, full.tile_eptr, tile_dense.p, tpos.p, epos.p, nb, T, d_tile_ptr.p, d_tile_col.p,
+        d_tile_eptr.p);
+    check(cudaGetLastError(), "hybrid_dense_kernel");
+    // residual part
+    Buf<uint64_t> r_key(size_t(std::max<int64_t>(R, 1))), r_skey(size_t(std::max<int64_t>(R, 1)));
+    Buf<unsigned short> r_val(size_t(std::max<int64_t>(R, 1))), r_sval(size_t(std::max<int64_t>(R, 1)));
+    if (nnz > 0) {
+        hybrid_entries_kernel<<<blocks_for(nnz), 256, 0, st>>>(full.ents, ent_dense.p, ent_tile.p, epos.p, tile_band.p,
+                                                               full.tile_col, H, nnz, d_ents.p, r_key.p, r_val.p);
+        check(cudaGetLastError(), "hybrid_entries_kernel");
+    }
+    Buf<int> bad(1);
+    check(cudaMemsetAsync(bad.p, 0, sizeof(int), st), "cudaMemsetAsync");
+    if (nb > 0) {
+        validate_dense_band_kernel<<<blocks_for(nb), 256, 0, st>>>(d_tile_ptr.p, d_tile_col.p, d_tile_eptr.p, nb, TD,
+                                                                   D, bad.p);
+        check(cudaGetLastError(), "validate_dense_band_kernel");
+    }
+    if (read_one(bad.p, st) != 0) throw StatusError(VCSRMC_INTERNAL, "hybrid dense band layout is inconsistent");
+    Buf<int> rp(size_t(M) + 1), rcols(size_t(std::max<int64_t>(R, 1))), row_count(size_t(M) + 1);
+    check(cudaMemsetAsync(row_count.p, 0, sizeof(int) * (size_t(M) + 1), st), "cudaMemsetAsync");
+    if (R > 0) {
+        int end_bit = 33;
+        while (end_bit < 64 && (uint64_t(uint32_t(M)) << 32) >> end_bit) ++end_bit;
+        size_t tmp = 0;
+        check(cub::DeviceRadixSort::SortPairs(nullptr, tmp, r_key.p, r_skey.p, r_val.p, r_sval.p, R, 0, end_bit, st),
+              "cub sort");
+        Buf<uint8_t> t(tmp);
+        check(cub::DeviceRadixSort::SortPairs(t.p, tmp, r_key.p, r_skey.p, r_val.p, r_sval.p, R, 0, end_bit, st),
+              "cub sort");
+        hybrid_resid_kernel<<<blocks_for(R), 256, 0, st>>>(r_skey.p, R, rcols.p, row_count.p);
+        check(cudaGetLastError(), "hybrid_resid_kernel");
+    }
+    exclusive_scan(row_count.p, rp.p, int64_t(M) + 1, st);
+    // work units over the non-empty rows, packed on the host from row_ptr alone
+    std::vector<int> hrp(size_t(M) + 1);
+    check(cudaMemcpyAsync(hrp.data(), rp.p, sizeof(int) * (size_t(M) + 1), cudaMemcpyDeviceToHost, st),
+          "cudaMemcpyAsync");
+    check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    if (hrp[size_t(M)] != R) throw StatusError(VCSRMC_INTERNAL, "hybrid residual rows are inconsistent");
+    std::vector<RowViewHost::Unit> hunits;
+    std::vector<int> hsplit;
+    pack_units(hrp.data(), M, unit_nnz, hunits, hsplit, true);
+    Buf<int4> units(hunits.size());
+    Buf<int> split(hsplit.size());
+    if (!hunits.empty())
+        check(cudaMemcpyAsync(units.p, hunits.data(), sizeof(int4) * hunits.size(), cudaMemcpyHostToDevice, st),
+              "cudaMemcpyAsync");
+    if (!hsplit.empty())
+        check(cudaMemcpyAsync(split.p, hsplit.data(), sizeof(int) * hsplit.size(), cudaMemcpyHostToDevice, st),
+              "cudaMemcpyAsync");
+    RowsLayout rl;
+    rl.rp = rp.p;
+    rl.cols = rcols.p;
+    rl.units = units.p;
+    rl.n_units = int64_t(hunits.size());
+    if (!device_validate(nullptr, &rl, M, N, 16, st))
+        throw StatusError(VCSRMC_INTERNAL, "hybrid residual rows failed their index checks");
+    out.dense.band_rows = H;
+    out.dense.n_bands = nb;
+    out.dense.n_tiles = TD;
+    out.dense.tile_ptr = d_tile_ptr.release();
+    out.dense.tile_col = d_tile_col.release();
+    out.dense.tile_eptr = d_tile_eptr.release();
+    out.dense.ents = d_ents.release();
+    out.resid.rp = rp.release();
+    out.resid.cols = rcols.release();
+    out.resid.vals = r_sval.release();
+    out.resid.units = units.release();
+    out.resid.n_units = int64_t(hunits.size());
+    out.resid.split_rows = split.release();
+    out.resid.n_split_rows = int(hsplit.size());
+    return out;
+}
+
 // ---- hot columns of the ROWS plan ------------------------------------------------------------
 namespace {
 

@@ -75,6 +75,19 @@ BandChoice choose_band_device(const int* row_ptr, const int* col, int M, cudaStr
 BandLayout build_band_layout(const int* row_ptr, const int* col, const float* val, int M, int64_t nnz, float scale,
                              int band_rows, cudaStream_t st);
 
+// HYBRID plan from a full band layout `full` of the matrix (build_band_layout): the tiles with at
+// least min_entries entries as a band layout of their own (tiles and entries compacted in order, so
+// it equals the band view the host builds from the dense entries), and every other entry as a row
+// view (rows ascending, columns ascending in a row, fp16 values; units packed over non-empty rows
+// for accumulate-only use). `full` is left as it is. Throws StatusError on failure (nothing leaked).
+struct HybridLayout {
+    BandLayout dense;
+    RowsLayout resid;
+    int64_t dense_nnz = 0, resid_nnz = 0;
+};
+HybridLayout build_hybrid_layout(const BandLayout& full, int M, int N, int64_t nnz, int min_entries, int unit_nnz,
+                                 cudaStream_t st);
+
 // Checks the invariants the SpMM kernels rely on (index ranges, offsets, item ranges). Blocking.
 bool device_validate(const SegmentLayout* seg, const RowsLayout* rows, int M, int N, int segw, cudaStream_t st);
 

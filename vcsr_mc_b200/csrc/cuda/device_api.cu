@@ -741,12 +741,12 @@ VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const i
         for (int r : o.reserved)
             if (r != 0) throw StatusError(VCSRMC_INVALID_ARG, "reserved upload options must be 0");
         int plans = o.plans == 0 ? ((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS)) : o.plans;
-        if (plans & ~((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS) | (1 << VCSRMC_PLAN_BAND)))
+        constexpr int kTensorPlans = (1 << VCSRMC_PLAN_BAND) | (1 << VCSRMC_PLAN_HYBRID);
+        if (plans & ~((1 << VCSRMC_PLAN_SEGMENT) | (1 << VCSRMC_PLAN_ROWS) | kTensorPlans))
             throw StatusError(VCSRMC_INVALID_ARG, "unknown plan bits");
-        if ((plans & (1 << VCSRMC_PLAN_BAND)) && fp32)
-            throw StatusError(VCSRMC_INVALID_ARG, "the BAND plan runs on the tensor cores and needs the FP16 format");
-        if (plans & (1 << VCSRMC_PLAN_HYBRID))
-            throw StatusError(VCSRMC_INVALID_ARG, "the HYBRID layout is built at upload (vcsrmc_upload_ex), not here");
+        if ((plans & kTensorPlans) && fp32)
+            throw StatusError(VCSRMC_INVALID_ARG,
+                              "the BAND and HYBRID plans run on the tensor cores and need the FP16 format");
         int unit_nnz = o.rows_unit_nnz;
         if (unit_nnz != 0 && (unit_nnz < 16 || unit_nnz > dev::kUnitNnzMax || (unit_nnz & (unit_nnz - 1))))
             throw StatusError(VCSRMC_INVALID_ARG, "rows_unit_nnz must be 0 or a power of two in [16, 1024]");
@@ -763,11 +763,13 @@ VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const i
         const float scale = fp32 ? 1.0f : half_scale_from_absmax(dev::device_abs_max(val, nnz, st));
         // The band height, and for the default plans whether BAND joins them (as for an upload).
         int band_rows = o.band_rows;
-        if ((band_rows == 0 && (plans & (1 << VCSRMC_PLAN_BAND))) || (o.plans == 0 && !fp32)) {
+        if ((band_rows == 0 && (plans & kTensorPlans)) || (o.plans == 0 && !fp32)) {
             const dev::BandChoice bc = dev::choose_band_device(row_ptr, col, M, st);
             if (band_rows == 0) band_rows = bc.band_rows;
             if (o.plans == 0 && !fp32 && bc.entries_per_tile >= dev::kBandMinEntriesPerTile)
                 plans |= 1 << VCSRMC_PLAN_BAND;
+            else if (o.plans == 0 && !fp32 && bc.dense_fraction >= dev::kHybridMinDenseFraction)
+                plans |= 1 << VCSRMC_PLAN_HYBRID;
         }
         auto* d = new vcsrmc_device_format;
         d->device = device;
@@ -813,8 +815,9 @@ VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const i
             if (!dev::device_validate(d->has_segment ? &seg : nullptr, d->has_rows ? &rows : nullptr, M, N, segw, st))
                 throw StatusError(VCSRMC_INTERNAL, "device-built format failed its index checks");
             make_hot_columns(d, nnz, o, st);
-            if (plans & (1 << VCSRMC_PLAN_BAND)) {
+            if (plans & kTensorPlans) {
                 dev::BandLayout band = dev::build_band_layout(row_ptr, col, val, M, nnz, scale, band_rows, st);
+                // the handle owns the full band layout from here (freed with it if BAND is not kept)
                 d->band_rows = band.band_rows;
                 d->n_bands = band.n_bands;
                 d->n_tiles = band.n_tiles;
@@ -822,7 +825,45 @@ VCSRMC_EXPORT int vcsrmc_build_device(int32_t M, int32_t N, int64_t nnz, const i
                 d->tile_col = band.tile_col;
                 d->tile_eptr = band.tile_eptr;
                 d->ents = band.ents;
-                d->has_band = true;
+                if (plans & (1 << VCSRMC_PLAN_HYBRID)) {
+                    if (unit_nnz == 0) {
+                        int sms = 0;
+                        cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device),
+                                   "cudaDeviceGetAttribute");
+                        unit_nnz = dev::choose_unit_nnz(nnz, sms);
+                    }
+                    dev::HybridLayout h = dev::build_hybrid_layout(band, M, N, nnz, int(dev::kBandMinEntriesPerTile),
+                                                                   unit_nnz, st);
+                    d->hb_rows = h.dense.band_rows;
+                    d->hb_bands = h.dense.n_bands;
+                    d->hb_tiles = h.dense.n_tiles;
+                    d->hb_nnz = h.dense_nnz;
+                    d->hb_tile_ptr = h.dense.tile_ptr;
+                    d->hb_tile_col = h.dense.tile_col;
+                    d->hb_tile_eptr = h.dense.tile_eptr;
+                    d->hb_ents = h.dense.ents;
+                    d->hr_nnz = h.resid_nnz;
+                    d->hr_rp = h.resid.rp;
+                    d->hr_cols = h.resid.cols;
+                    d->hr_vals = h.resid.vals;
+                    d->hr_units = h.resid.units;
+                    d->hr_n_units = h.resid.n_units;
+                    d->hr_split = h.resid.split_rows;
+                    d->hr_n_split = h.resid.n_split_rows;
+                    d->has_hybrid = true;
+                }
+                if (plans & (1 << VCSRMC_PLAN_BAND)) {
+                    d->has_band = true;
+                } else {
+                    cudaFree(d->tile_ptr);
+                    cudaFree(d->tile_col);
+                    cudaFree(d->tile_eptr);
+                    cudaFree(d->ents);
+                    d->tile_ptr = d->tile_col = d->tile_eptr = nullptr;
+                    d->ents = nullptr;
+                    d->band_rows = d->n_bands = 0;
+                    d->n_tiles = 0;
+                }
             }
             cuda_check(cudaMalloc(&d->status, sizeof(uint32_t)), "cudaMalloc");
             cuda_check(cudaMemsetAsync(d->status, 0, sizeof(uint32_t), st), "cudaMemsetAsync");

@@ -38,26 +38,28 @@ namespace dev {
 namespace {
 
 // Build-time shape of vcsr_rows_kernel: warps per block, the minimum resident blocks per SM the
-// register budget is sized for (0: not given; giving 1 already changes the compiler's
-// allocation), B gathers in flight per lane. Gathers in flight per SM decide its speed: on the
-// 2^24-row R-MAT, 4-warp blocks held to 72 registers (7 blocks = 28 warps per SM) run in
-// 9.65 ms against 10.50 ms for 8-warp blocks at 80 registers (24 warps), and 16 gathers in flight
-// per lane at 128 registers (16 warps) in 11.21 ms.
+// register budget is sized for (per B element type), B gathers in flight per lane. Gathers in
+// flight per SM decide its speed. On the 2^24-row R-MAT with fp16 B: 4-warp blocks whose A values
+// are read back from shared memory at their FMA, held to 64 registers (8 blocks = 32 warps per SM),
+// run in 9.30 ms, against 10.24 ms for the same blocks holding the 8 A values in registers at 72
+// registers (7 blocks), and 10.50 ms for 8-warp blocks at 80 registers; 16 gathers in flight per
+// lane at 128 registers (16 warps) took 11.21 ms. With fp32 B the 64-register build lost (16.29
+// against 15.21 ms), so fp32 B keeps 7 blocks of 72 registers.
 #ifndef VCSRMC_ROWS_WARPS
 #define VCSRMC_ROWS_WARPS 4
-#endif
-#ifndef VCSRMC_ROWS_MIN_BLOCKS
-#define VCSRMC_ROWS_MIN_BLOCKS 7
-#endif
-#if VCSRMC_ROWS_MIN_BLOCKS > 0
-#define VCSRMC_ROWS_BOUNDS __launch_bounds__(VCSRMC_ROWS_WARPS * 32, VCSRMC_ROWS_MIN_BLOCKS)
-#else
-#define VCSRMC_ROWS_BOUNDS __launch_bounds__(VCSRMC_ROWS_WARPS * 32)
 #endif
 #ifndef VCSRMC_ROWS_IN_FLIGHT
 #define VCSRMC_ROWS_IN_FLIGHT 8
 #endif
 constexpr int kWarpsPerBlock = VCSRMC_ROWS_WARPS;
+// Resident blocks per SM that the register budget of vcsr_rows_kernel is sized for, and whether
+// the staged A values are read back from shared memory at their FMA (instead of held in registers
+// while the gathers are in flight), by B element size.
+template <typename BT>
+struct RowsShape {
+    static constexpr int kMinBlocks = sizeof(BT) == 2 ? 8 : 7;
+    static constexpr bool kReloadA = sizeof(BT) == 2;
+};
 constexpr int kFoldedWarpsPerBlock = 8;  // vcsr_rows_folded_kernel (narrow B)
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -198,7 +200,7 @@ static_assert(kInFlight == 8 || kInFlight == 16, "a batch of 16 entries in round
 // and gathers B eight entries at a time; runs of eight entries without a row end skip the
 // per-entry row-end test.
 template <bool kVec, bool kAccumulate, typename VT, typename BT>
-__global__ void VCSRMC_ROWS_BOUNDS
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks)
     vcsr_rows_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
                      const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
                      int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale,
@@ -274,22 +276,28 @@ __global__ void VCSRMC_ROWS_BOUNDS
         __syncwarp(gmask);
         for (int j = 0; j < n; j += kInFlight) {
             uint4 raw[kInFlight];
-            uint32_t av[kInFlight];
+            uint32_t av[kInFlight];  // held only when RowsShape<BT>::kReloadA is false
 #pragma unroll
             for (int k = 0; k < kInFlight; ++k) {
                 const Staged e = stage[j + k];
-                av[k] = e.v;
+                if constexpr (!RowsShape<BT>::kReloadA) av[k] = e.v;
                 const BT* p = reinterpret_cast<const BT*>(bbase + e.off);
                 raw[k] = e.once ? load16_once<kVec>(p, nv) : load16<kVec>(p, nv);
             }
+            // A value of entry j + k at its FMA: from shared memory (8 registers fewer held while the
+            // gathers are in flight) or from the registers loaded with the gathers
+            auto a_of = [&](int k) -> uint32_t {
+                if constexpr (RowsShape<BT>::kReloadA) return stage[j + k].v;
+                else return av[k];
+            };
             const unsigned eb = (ends >> j) & ((1u << kInFlight) - 1u);
             if (eb == 0) {
 #pragma unroll
-                for (int k = 0; k < kInFlight; ++k) fma_lane<VT, BT>(acc, av[k], raw[k]);
+                for (int k = 0; k < kInFlight; ++k) fma_lane<VT, BT>(acc, a_of(k), raw[k]);
             } else {
 #pragma unroll
                 for (int k = 0; k < kInFlight; ++k) {
-                    fma_lane<VT, BT>(acc, av[k], raw[k]);
+                    fma_lane<VT, BT>(acc, a_of(k), raw[k]);
                     if ((eb >> k) & 1u) {
                         const int row = rb + __shfl_sync(gmask, lo, j + k, kL);
                         write_lane<kE, kVec, kOut>(C + int64_t(row) * ldc + c0, acc, scale, nv);
