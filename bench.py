@@ -645,21 +645,28 @@ def main() -> None:
             return a.elapsed_time(b)
 
         up_ms, down_ms, both_ms = copy_ms(True, False), copy_ms(False, True), copy_ms(True, True)
-        link = torch.tensor([up_ms, down_ms, both_ms], dtype=torch.float64, device="cuda")
+        h2d_b, d2h_b = hB.numel() * hB.element_size(), hC.numel() * hC.element_size()
+        # per rank: its copy times and rates; the job's step takes the slowest rank's, and its bytes
+        # are the sum over ranks
+        local = torch.tensor([up_ms, down_ms, both_ms, -h2d_b / max(up_ms, 1e-6) * 1e-6,
+                              -d2h_b / max(down_ms, 1e-6) * 1e-6], dtype=torch.float64, device="cuda")
+        total = torch.tensor([float(h2d_b), float(d2h_b)], dtype=torch.float64, device="cuda")
         if dist is not None:
-            dist.all_reduce(link, op=dist.ReduceOp.MAX)
-        up_ms, down_ms, both_ms = (float(x) for x in link.tolist())
+            dist.all_reduce(local, op=dist.ReduceOp.MAX)
+            dist.all_reduce(total, op=dist.ReduceOp.SUM)
+        up_ms, down_ms, both_ms, up_rate, down_rate = (float(x) for x in local.tolist())
         e2e = {"value": flops / (float(e2e_ms) * 1e-3) / 1e9, "unit": "GFLOP/s",
-               "h2d_bytes_per_step": int(hB.numel() * hB.element_size()),
-               "d2h_bytes_per_step": int(hC.numel() * hC.element_size()), "ms_per_step": float(e2e_ms),
+               "h2d_bytes_per_step": int(total[0]), "d2h_bytes_per_step": int(total[1]),
+               "bytes_scope": "summed over ranks" if world > 1 else "one rank",
+               "ms_per_step": float(e2e_ms),
                "pipelining": "upload of step i+1 overlaps download of step i (two device buffers, two copy streams)",
                "steps": args.e2e_steps,
                "link": {"h2d_ms": up_ms, "d2h_ms": down_ms, "both_ms": both_ms,
-                        "h2d_GBps": hB.numel() * hB.element_size() / (max(up_ms, 1e-6) * 1e-3) / 1e9,
-                        "d2h_GBps": hC.numel() * hC.element_size() / (max(down_ms, 1e-6) * 1e-3) / 1e9,
+                        "h2d_GBps": -up_rate, "d2h_GBps": -down_rate,
                         "floor_ms_per_step": both_ms,
                         "frac": both_ms / max(float(e2e_ms), 1e-6),
-                        "how": "this step's H2D and D2H copies timed alone and at once, max over ranks"},
+                        "how": "this step's H2D and D2H copies of each rank timed alone and at once; times are "
+                               "the slowest rank's, GB/s the slowest rank's own bytes over its own time"},
                "b_staging": ("each rank uploads 1/N of B, NCCL all-gather over NVLink" if world > 1 else
                              "B uploaded whole"),
                "a_resident": True,

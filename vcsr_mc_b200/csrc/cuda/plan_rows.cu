@@ -59,6 +59,8 @@ template <typename BT>
 struct RowsShape {
     static constexpr int kMinBlocks = sizeof(BT) == 2 ? 8 : 7;
     static constexpr bool kReloadA = sizeof(BT) == 2;
+    // vcsr_rows_folded_kernel (8-warp blocks): 4 blocks = 64 registers for fp16 B; 0 = not given
+    static constexpr int kFoldedMinBlocks = sizeof(BT) == 2 ? 4 : 0;
 };
 constexpr int kFoldedWarpsPerBlock = 8;  // vcsr_rows_folded_kernel (narrow B)
 constexpr unsigned kFull = 0xffffffffu;
@@ -320,7 +322,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks
 // folds sharing a row are contiguous); a row that continues past a step is carried in every
 // lane's accumulator; the fold holding a row's last entry writes the row.
 template <int kF, bool kVec, bool kAccumulate, typename VT, typename BT>
-__global__ void __launch_bounds__(kFoldedWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kFoldedWarpsPerBlock * 32, RowsShape<BT>::kFoldedMinBlocks)
     vcsr_rows_folded_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
                             const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
                             int row_bytes, int O, float* __restrict__ C, int64_t ldc, float scale,
@@ -396,14 +398,18 @@ __global__ void __launch_bounds__(kFoldedWarpsPerBlock * 32)
         __syncwarp(gmask);
         for (int t0 = 0; t0 < kSteps; t0 += kR) {
             uint4 raw[kR];
-            uint32_t av[kR];
+            uint32_t av[kR];  // held only when RowsShape<BT>::kReloadA is false
 #pragma unroll
             for (int k = 0; k < kR; ++k) {
                 const Staged e = stage[(t0 + k) * kF + fold];
-                av[k] = e.v;
+                if constexpr (!RowsShape<BT>::kReloadA) av[k] = e.v;
                 const BT* p = reinterpret_cast<const BT*>(bbase + e.off);
                 raw[k] = e.once ? load16_once<kVec>(p, nv) : load16<kVec>(p, nv);
             }
+            auto a_of = [&](int k) -> uint32_t {
+                if constexpr (RowsShape<BT>::kReloadA) return stage[(t0 + k) * kF + fold].v;
+                else return av[k];
+            };
 #pragma unroll
             for (int k = 0; k < kR; ++k) {
                 const int j0 = (t0 + k) * kF;  // first entry of this step
@@ -411,7 +417,7 @@ __global__ void __launch_bounds__(kFoldedWarpsPerBlock * 32)
 #pragma unroll
                 for (int g = 0; g < kF; ++g) row[g] = __shfl_sync(gmask, lo, j0 + g, kL);
                 float c[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                fma_lane<VT, BT>(c, av[k], raw[k]);
+                fma_lane<VT, BT>(c, a_of(k), raw[k]);
                 float v[8];
                 const bool carry_in = row[fold] == open_row;
 #pragma unroll
