@@ -107,14 +107,19 @@ def test_rows_unit_sizes(cuda, unit_nnz, fp32, accumulate):
 @pytest.mark.parametrize("fp32", [True, False], ids=["fp32", "fp16"])
 @pytest.mark.parametrize("O", [1, 8, 16, 24, 32, 33, 48, 64, 65])
 @pytest.mark.parametrize("accumulate", [False, True], ids=["store", "accumulate"])
-def test_rows_narrow_widths(cuda, O, fp32, accumulate):
-    """ROWS plan on narrow B, where 2 or 4 entries share a lane group (rows split across folds and
-    steps, heavy-row chunks reduced into C)."""
+@pytest.mark.parametrize("aligned", [True, False], ids=["aligned", "unaligned"])
+def test_rows_narrow_widths(cuda, O, fp32, accumulate, aligned):
+    """ROWS plan on narrow B: with 16-byte aligned rows the main kernel (idle lanes masked); with
+    unaligned rows the element-wise path, where 2 or 4 entries share a lane group for O <= 64
+    (rows split across folds and steps, heavy-row chunks reduced into C)."""
     A = vm.CSR.generate(vm.GEN_ZIPF, 1 << 14, seed=7)
     B = np.random.default_rng(O).uniform(-1, 1, size=(A.N, O)).astype(np.float32)
     base = np.random.default_rng(8).uniform(-1, 1, size=(A.M, O)).astype(np.float32) if accumulate else None
+    elem = 4 if fp32 else 2
+    # pad B's rows so that their pitch is (or is not) a multiple of 16 bytes
+    pad = next(p for p in range(16) if (((O + p) * elem) % 16 == 0) == aligned)
     C, Bu = run_gpu(cuda, A, B, fp32, 32, 64, b_half=not fp32, accumulate_into=base, plan=vm.PLAN_ROWS,
-                    unit_nnz=32)
+                    unit_nnz=32, ldb_pad=pad)
     oracle_check(A, C, Bu, fp32, base=None if base is None else base.astype(np.float64))
 
 

@@ -143,7 +143,11 @@ __device__ __forceinline__ uint32_t a_bits(const VT* p) {
     }
 }
 
-// C row segment of this lane: kE columns at dst (nv valid). Overwrite, add, or reduce.
+// C row segment of this lane: kE columns at dst (nv valid). Overwrite, add, or reduce. A row of C
+// belongs to one lane group (or, split into chunks, is reduced by several): adding into it is a
+// fire-and-forget vector reduction (red.global.add.v4.f32), one fp32 add of the row's sum to the
+// old value as a load-add-store would do, without waiting for the old value at every row end
+// (accumulate mode, config 4: 10.15 -> 8.49 ms; config-2 matrix, O = 16-128: 22-31 % faster).
 enum class RowOut { kStore, kAdd, kReduce };
 template <int kE, bool kVec, RowOut kOut>
 __device__ __forceinline__ void write_lane(float* dst, const float (&acc)[8], float scale, int nv) {
@@ -155,21 +159,13 @@ __device__ __forceinline__ void write_lane(float* dst, const float (&acc)[8], fl
         for (int i = 0; i < kE; i += 4) {
             float4 x = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
             float4* d4 = reinterpret_cast<float4*>(dst + i);
-            if constexpr (kOut == RowOut::kReduce) {
-                atomicAdd(d4, x);
-            } else {
-                if constexpr (kOut == RowOut::kAdd) {
-                    const float4 o = *d4;
-                    x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
-                }
-                __stcs(d4, x);
-            }
+            if constexpr (kOut == RowOut::kStore) __stcs(d4, x);
+            else atomicAdd(d4, x);
         }
     } else {
         for (int i = 0; i < nv; ++i) {
-            if constexpr (kOut == RowOut::kReduce) atomicAdd(dst + i, v[i]);
-            else if constexpr (kOut == RowOut::kAdd) dst[i] += v[i];
-            else dst[i] = v[i];
+            if constexpr (kOut == RowOut::kStore) dst[i] = v[i];
+            else atomicAdd(dst + i, v[i]);
         }
     }
 }
@@ -314,7 +310,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks
     if (partial) write_lane<kE, kVec, RowOut::kReduce>(C + int64_t(rb) * ldc + c0, acc, scale, nv);
 }
 
-// The same plan for narrow B (O <= 64 fp16 or O <= 32 fp32 columns... in general O <= kL * kE / 2):
+// The same plan for narrow B on the element-wise path (O <= kL * kE / 2 columns: 64 fp16, 64 fp32):
 // a row slice of B then needs only kW = kL / kF lanes, so each lane group works on kF entries at
 // once. Fold f of the group (lanes f * kW .. f * kW + kW - 1) takes entries f, f + kF, f + 2 kF, ...
 // of every staged batch. Per step of kF consecutive entries the folds' contributions to the same
@@ -545,13 +541,18 @@ cudaError_t launch_rows_t(const RowPlanView& P, const BT* B, int64_t ldb, int O,
     }
     const int* hot_cols = P.hot.hot_cols;
     const int cold_hint = (P.hot.n_hot > 0 && P.hot.cold_hint) ? 1 : 0;
-    // narrow B: fold 4 or 2 entries into one lane group when a row slice fits a quarter or half
-    if (O <= kL * kE / 4) {
+    // Narrow B on the element-wise path (B or C rows not 16-byte aligned): fold 4 or 2 entries into
+    // one lane group when a row slice fits a quarter or half of it. With 16-byte loads the main
+    // kernel is faster at every width, its idle lanes included (config-2 matrix, O = 8..64, store
+    // mode: fp16 B 0.108-0.112 ms against 0.114-0.136 ms folded, fp32 B 0.140-0.151 against
+    // 0.153-0.177 ms; accumulate mode with reductions: fp16 B 0.098-0.102 against 0.119-0.148 ms);
+    // on the element-wise path folding wins (O = 33: 0.196 against 0.218 ms).
+    if (!kVec && O <= kL * kE / 4) {
         LaunchShape L(dim3(unsigned(fblocks)), dim3(kFoldedWarpsPerBlock * 32), st, window, window_bytes);
         return cudaLaunchKernelEx(&L.cfg, vcsr_rows_folded_kernel<4, kVec, kAcc, VT, BT>, P.units, P.n_units, P.rp,
                                   P.cols, vals, B, row_bytes, O, C, ldc, P.scale, hot_cols, k_copy, hot_delta, cold_hint);
     }
-    if (O <= kL * kE / 2) {
+    if (!kVec && O <= kL * kE / 2) {
         LaunchShape L(dim3(unsigned(fblocks)), dim3(kFoldedWarpsPerBlock * 32), st, window, window_bytes);
         return cudaLaunchKernelEx(&L.cfg, vcsr_rows_folded_kernel<2, kVec, kAcc, VT, BT>, P.units, P.n_units, P.rp,
                                   P.cols, vals, B, row_bytes, O, C, ldc, P.scale, hot_cols, k_copy, hot_delta, cold_hint);
