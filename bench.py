@@ -394,9 +394,10 @@ def main() -> None:
                                "is the CSR itself with fp16 values, so this is a CSR SpMM; the VCSR-MC arrays feed the "
                                "SEGMENT/BAND plans and validation), C stored once",
                        "segment": "segment: reference dataflow, per-item B segment, C reductions",
-                       "band": "band: 128-row bands x {band_cols}-column tiles on tcgen05, TMEM accumulator, C stored once",
-                       "hybrid": "hybrid: band tiles with >= 64 entries on tcgen05 (C stored once), the other entries "
-                                 "on the rows plan added into C"}[args.plan],
+                       "band": "band: {band_rows}-row bands x {band_cols}-column tiles on tcgen05 (transposed product, "
+                               "MMA M = 128 columns of C, N = {band_n} band rows), TMEM accumulator, C stored once",
+                       "hybrid": "hybrid: band tiles ({hybrid_rows}-row bands) with >= 64 entries on tcgen05 (C stored "
+                                 "once), the other entries on the rows plan added into C"}[args.plan],
               "parallelism": f"row-shard x{args.gpus} (balanced on nnz + {args.row_weight} x rows), B replicated",
               "l2": None}
 
@@ -479,7 +480,9 @@ def main() -> None:
         (1 if plan == vm.PLAN_ROWS and info["n_split_rows"] > 0 else 0) + \
         (1 if plan == vm.PLAN_ROWS and info["n_hot"] > 0 and args.hot_budget_mib > 0 else 0)
     groups, slots, items = info["n_groups"], info["n_slots"], info["n_items"]
-    config["plan"] = config["plan"].format(band_cols=info["band_cols"])
+    config["plan"] = config["plan"].format(band_cols=info["band_cols"], band_rows=info["band_rows"],
+                                           band_n=64 if info["band_rows"] <= 64 else 128,
+                                           hybrid_rows=info["hybrid_band_rows"])
     log(f"rank {rank}: rows [{r0},{r1}) nnz {p1 - p0} format build + upload ({args.build}) {build_s:.2f}s "
         f"setup {time.time() - t0:.1f}s")
 

@@ -182,11 +182,11 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
     return d;
 }
 
-// Instruction descriptor for kind::f16 with fp16 A/B, fp32 D, A K-major, B K- or MN-major.
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major) {
+// Instruction descriptor for kind::f16 with fp16 A/B, fp32 D; A and B each K- or MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major, bool a_mn_major = false) {
     return (1u << 4)                        // D format: f32
            | (0u << 7) | (0u << 10)          // A, B format: f16
-           | (0u << 15)                      // A K-major
+           | ((a_mn_major ? 1u : 0u) << 15)  // A major
            | ((b_mn_major ? 1u : 0u) << 16)  // B major
            | (uint32_t(N >> 3) << 17)        // N / 8
            | (uint32_t(M >> 4) << 24);       // M / 16

@@ -7,22 +7,25 @@
 // same tcgen05 tile product (A densified from (column, value) entries in shared memory, B staged
 // by TMA with the 128-byte swizzle, fp32 accumulation) runs row-stationary:
 //   * a tile = a band's entries in kBandK (64) consecutive columns starting at the first column
-//     not covered by the previous tile; each adds a (band x 64) by (64 x 128) product into the
-//     band's TMEM accumulator (M = 128, N = 128, four K = 16 steps);
-//   * persistent CTAs (two per SM) walk their work items (band, slab) in a strided order; the
-//     tiles of all their items form one sequence through 3 shared-memory stages (B 16 KB, A
-//     16 KB). Producer warp w owns stage w: once the MMAs of its previous tile have completed it
-//     starts the TMA load of its next B tile, prefetches the one after into L2, clears its
-//     previous entries from the A tile (the positions it remembers, or the whole tile after a
-//     large one), writes the new entries and arrives on the stage's barrier. Its registers run
-//     one position ahead (entries and bounds are loaded two iterations before use);
+//     not covered by the previous tile; each adds its product into the band's TMEM accumulator,
+//     transposed: (128 slab columns x 64) by (64 x NB band rows), NB = 64 for bands of at most 64
+//     rows, else 128 (M = 128, N = NB, four K = 16 steps);
+//   * persistent CTAs (three per SM for NB = 64, two for NB = 128) walk their work items (band,
+//     slab) in a strided order; the tiles of all their items form one sequence through the CTA's
+//     shared-memory stages (B 16 KB + A NB x 128 bytes each). Producer warp w owns stage w: once
+//     the MMAs of its previous tile have completed it starts the TMA load of its next B tile,
+//     prefetches the one after into L2, clears its previous entries from the A tile (the positions
+//     it remembers, or the whole tile after a large one), writes the new entries and arrives on
+//     the stage's barrier. Its registers run one position ahead (entries and bounds are loaded two
+//     iterations before use);
 //   * lane 0 of the MMA warp issues the MMAs in sequence order into one of two TMEM
-//     accumulators (256 columns), so the MMAs of a band overlap the epilogue of the previous one;
-//   * four epilogue warps read their TMEM lane quarter (tcgen05.ld), transpose 32 x 16 blocks
-//     through shared memory and write C in whole 32-byte sectors (read once for C += A*B).
-// Two CTAs per SM outrun one CTA with twice the stages (0.300 against 0.365 ms on a 27-point
-// stencil): each CTA's MMA issuer walks its tiles one at a time, and the second CTA fills its
-// waits. 64-column tiles beat 32-column ones (0.317 ms) by halving the tiles.
+//     accumulators, so the MMAs of a band overlap the epilogue of the previous one;
+//   * four epilogue warps read their TMEM lane quarter (tcgen05.ld: a lane is a column of C, the
+//     registers are rows) and store each row's 32 columns as one 128-byte warp store (read once
+//     for C += A*B).
+// Several CTAs per SM outrun one CTA with more stages (0.300 against 0.365 ms on a 27-point
+// stencil in an earlier form): each CTA's MMA issuer walks its tiles one at a time, and the other
+// CTAs fill its waits. 64-column tiles beat 32-column ones by halving the tiles.
 // B traffic per band is the B rows of its tiles (64 x 256 bytes each), which neighbouring bands
 // share in L2; this suits matrices whose rows touch few column windows (stencils, banded or
 // reordered matrices). Matrices with scattered columns are served better by the ROWS plan.
@@ -46,50 +49,59 @@ namespace vcsrmc {
 namespace dev {
 namespace {
 
-// Build-time shape: stages per CTA and CTAs per SM share the SM's shared memory (a stage holds a
-// kBandK-row B tile and a 128 x kBandK A tile).
-#ifndef VCSRMC_BAND_STAGES
-#define VCSRMC_BAND_STAGES (kBandK == 64 ? 3 : 5)
-#endif
-#ifndef VCSRMC_BAND_CTAS
-#define VCSRMC_BAND_CTAS 2
-#endif
-constexpr int kSlab = 128;                       // columns of B and C per work item = MMA N
-constexpr int kStages = VCSRMC_BAND_STAGES;
-constexpr int kProducers = kStages;              // warps 0 .. kStages - 1: producer w fills stage w
-constexpr int kMmaWarp = kProducers;             // next warp: lane 0 issues the MMAs
-constexpr int kEpiWarp0 = kProducers + 1;        // last 4 warps: epilogue (TMEM lane quarter = warp % 4)
-constexpr int kWarps = kEpiWarp0 + 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kCtasPerSm = VCSRMC_BAND_CTAS;
+// The band product, for bands of at most NB rows (64 or 128): D^T (128 slab columns x NB band rows)
+// = B tile^T (M = 128, MN-major: kBandK rows of B x 128 columns in two 64-column panels with the
+// 128-byte swizzle, as TMA lands them) x A tile^T (N = NB, K-major: the band's entries scattered
+// into NB x kBandK fp16). A TMEM lane holds a column of C, so a warp's store of one row writes 128
+// contiguous bytes, and a band of at most 64 rows costs half the tensor-core work of N = 128.
+// Per SM, stages in flight decide the speed (each stage waits for its B tile's TMA load after its
+// previous MMAs complete): on a 27-point stencil at 62-row bands, 2 CTAs x 3 stages took 0.298 ms,
+// 2 x 4 stages 0.278 ms and 3 x 3 stages 0.2665 ms; 128-row bands (2 x 3 stages) 0.289 ms, against
+// 0.294 ms for the same product with a row of C per TMEM lane and a transposing epilogue.
+constexpr int kSlab = 128;                       // columns of B and C per work item (= MMA M)
 constexpr int kSaved = 8;                        // entries a producer lane keeps per tile (to clear them)
 constexpr int kAccs = 2;                         // TMEM accumulators: one band's MMAs overlap the previous epilogue
-constexpr uint32_t kTmemCols = kAccs * kSlab;
 constexpr int kPanelBytes = kBandK * 128;        // kBandK rows x 64 fp16, 128-byte swizzle
 constexpr int kBBytes = 2 * kPanelBytes;
-constexpr int kABytes = kBandRows * kBandK * 2;
-constexpr int kStageBytes = kBBytes + kABytes;   // a multiple of 1024: swizzle atoms stay aligned
-// Epilogue staging: 32 rows x 16 columns of fp32 per warp, the 16-byte chunk j of row r at
-// chunk position j ^ ((r >> 1) & 3), so that both the row-per-lane writes and the
-// row-segment reads of a quarter warp touch 8 distinct 4-bank groups.
-constexpr int kEpiCols = 16;
-constexpr int kEpiBytes = 32 * kEpiCols * 4;
-constexpr int kEpiOffset = kStages * kStageBytes;
-constexpr int kBarOffset = kEpiOffset + 4 * kEpiBytes;
-constexpr int kNumBars = 3 * kStages + 2 * kAccs;
-constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // + barriers, slot, flag, alignment
-static_assert(kStageBytes % 1024 == 0, "stage alignment");
-static_assert(kCtasPerSm * kTmemCols <= 512, "tensor memory per SM");
-static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 233472, "shared memory per SM");
-static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+constexpr int kSmemPerSm = 233472;
+#ifndef VCSRMC_BAND_CTAS64
+#define VCSRMC_BAND_CTAS64 3
+#endif
+
+template <int NB>
+struct BandShape {
+    static_assert(NB == 64 || NB == 128, "bands of at most 64 or 128 rows");
+    static constexpr int kCtas = NB == 64 ? VCSRMC_BAND_CTAS64 : 2;  // CTAs per SM
+    static constexpr int kABytes = NB * kBandK * 2;
+    static constexpr int kStageBytes = kBBytes + kABytes;  // a multiple of 1024: swizzle atoms stay aligned
+    static constexpr int kFixed = (3 * 8 + 2 * kAccs) * 8 + 16 + 1024;  // barriers, slot, flag, alignment
+    static constexpr int kFit = (kSmemPerSm / kCtas - 1024 - kFixed) / kStageBytes;
+    static constexpr int kStages = kFit < 6 ? kFit : 6;
+    static constexpr int kProducers = kStages;   // warps 0 .. kStages - 1: producer w fills stage w
+    static constexpr int kMmaWarp = kProducers;  // next warp: lane 0 issues the MMAs
+    static constexpr int kEpiWarp0 = kProducers + 1;  // last 4 warps: epilogue (TMEM lane quarter = warp % 4)
+    static constexpr int kThreads = (kEpiWarp0 + 4) * 32;
+    static constexpr uint32_t kTmemCols = kAccs * NB;
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kNumBars = 3 * kStages + 2 * kAccs;
+    static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
+    static constexpr uint32_t kIdesc = idesc_f16_f32(kSlab, NB, false, true);  // A MN-major, B K-major
+    static_assert(kStages >= 2 && kStages <= 8, "two to eight stages");
+    static_assert(kStageBytes % 1024 == 0, "stage alignment");
+    static_assert(kCtas * kTmemCols <= 512, "tensor memory per SM");
+    static_assert(kCtas * (kSmemBytes + 1024) <= kSmemPerSm, "shared memory per SM");
+};
 
 // Byte offset of A element (row r, column c) in the K-major, unswizzled A tile: core matrices of
 // 8 rows x 16 bytes, K-adjacent ones 128 B apart (LBO), 8-row blocks kBandK * 16 B apart (SBO).
 __device__ __forceinline__ int a_offset(int r, int c) {
     return ((r >> 3) * (kBandK / 8) + (c >> 3)) * 128 + (r & 7) * 16 + (c & 7) * 2;
 }
+// An entry's place in an A tile of NB rows (the row masked to the tile, so that no entry can write
+// outside it).
+template <int NB>
 __device__ __forceinline__ int ent_offset(uint32_t e) {
-    return a_offset(int((e >> kBandColBits) & 127u), int(e & uint32_t(kBandK - 1)));
+    return a_offset(int((e >> kBandColBits) & uint32_t(NB - 1)), int(e & uint32_t(kBandK - 1)));
 }
 
 __device__ __forceinline__ __half to_half(float v) { return __float2half_rn(v); }
@@ -193,17 +205,18 @@ __device__ __forceinline__ void load_entries(ProducerRegs& r, const BandPlanView
     }
 }
 
-template <bool kTma, bool kAcc, typename BT>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+template <bool kTma, bool kAcc, typename BT, int NB>
+__global__ void __launch_bounds__(BandShape<NB>::kThreads, BandShape<NB>::kCtas)
     vcsr_band_kernel(BandPlanView P, const __grid_constant__ CUtensorMap tmap, const BT* __restrict__ B,
-                     int64_t ldb, int O, float* __restrict__ C, int64_t ldc, int vec_c) {
+                     int64_t ldb, int O, float* __restrict__ C, int64_t ldc) {
+    using S = BandShape<NB>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-    uint64_t* full_b = reinterpret_cast<uint64_t*>(smem + kBarOffset);  // B tile of a stage landed (TMA)
-    uint64_t* full_a = full_b + kStages;                                 // A tile of a stage written
-    uint64_t* done = full_a + kStages;                                   // MMAs reading a stage completed
-    uint64_t* acc_full = done + kStages;                                 // a band's accumulator is complete
+    uint64_t* full_b = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);  // B tile of a stage landed (TMA)
+    uint64_t* full_a = full_b + S::kStages;                                 // A tile of a stage written
+    uint64_t* done = full_a + S::kStages;                                   // MMAs reading a stage completed
+    uint64_t* acc_full = done + S::kStages;                                 // a band's accumulator is complete
     uint64_t* acc_empty = acc_full + kAccs;                              // the epilogue has read it
     uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + kAccs);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
@@ -212,12 +225,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const int n_items = P.n_bands * ((O + kSlab - 1) / kSlab);
 
     if (warp == 0) {
-        tmem_alloc(tslot, kTmemCols);
+        tmem_alloc(tslot, S::kTmemCols);
         tmem_relinquish();
     }
     if (tid == 0) {
 #pragma unroll
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < S::kStages; ++s) {
             mbar_init(&full_b[s], 1);
             mbar_init(&full_a[s], 1);
             mbar_init(&done[s], 1);
@@ -232,9 +245,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         if constexpr (kTma) prefetch_tmap(&tmap);
     }
     // A tiles start zeroed; afterwards a producer clears its previous tile's entries.
-    for (int i = tid; i < kStages * (kABytes / 16); i += kThreads) {
-        const int s = i / (kABytes / 16), j = i % (kABytes / 16);
-        reinterpret_cast<uint4*>(smem + s * kStageBytes + kBBytes)[j] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < S::kStages * (S::kABytes / 16); i += S::kThreads) {
+        const int s = i / (S::kABytes / 16), j = i % (S::kABytes / 16);
+        reinterpret_cast<uint4*>(smem + s * S::kStageBytes + kBBytes)[j] = make_uint4(0u, 0u, 0u, 0u);
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -242,10 +255,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
-    if (warp < kProducers) {
-        // ---- producer w: positions w, w + kStages, ... of the tile sequence, into stage w -----
+    if (warp < S::kProducers) {
+        // ---- producer w: positions w, w + S::kStages, ... of the tile sequence, into stage w -----
         const int s = warp;
-        uint8_t* Bs = smem + s * kStageBytes;
+        uint8_t* Bs = smem + s * S::kStageBytes;
         uint8_t* As = Bs + kBBytes;
         int saved[kSaved];
 #pragma unroll
@@ -262,14 +275,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         X.it = iter_begin(P, n_items, s);
         load_bounds(X, P, n_items);
         Y.it = X.it;
-        iter_advance(Y.it, kStages, P, n_items);
+        iter_advance(Y.it, S::kStages, P, n_items);
         load_bounds(Y, P, n_items);
         load_entries(X, P, lane);
         auto step = [&](ProducerRegs& cur, ProducerRegs& nxt, ProducerRegs& nn) -> bool {
             if (cur.it.item >= n_items) return false;
             load_entries(nxt, P, lane);
             nn.it = nxt.it;
-            iter_advance(nn.it, kStages, P, n_items);
+            iter_advance(nn.it, S::kStages, P, n_items);
             load_bounds(nn, P, n_items);
             // the stage is free once the MMAs of its previous tile completed (lane 0 waits; the
             // warp barrier orders the other lanes' writes to the stage after its observation)
@@ -302,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             // clear the previous tile's entries: the remembered ones, or the whole tile
             if (use > 0) {
                 if (prev_overflow) {
-                    for (int j = lane; j < kABytes / 16; j += 32)
+                    for (int j = lane; j < S::kABytes / 16; j += 32)
                         reinterpret_cast<uint4*>(As)[j] = make_uint4(0u, 0u, 0u, 0u);
                 } else {
 #pragma unroll
@@ -316,14 +329,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 const int e = cur.e0 + lane + 32 * k;
                 saved[k] = -1;
                 if (e < cur.e1) {
-                    saved[k] = ent_offset(cur.ev[k]);
+                    saved[k] = ent_offset<NB>(cur.ev[k]);
                     *reinterpret_cast<uint16_t*>(As + saved[k]) = uint16_t(cur.ev[k] >> 16);
                 }
             }
             prev_overflow = cur.e1 - cur.e0 > 32 * kSaved;
             for (int e = cur.e0 + 32 * kSaved + lane; e < cur.e1; e += 32) {
                 const uint32_t en = __ldg(P.ents + e);
-                *reinterpret_cast<uint16_t*>(As + ent_offset(en)) = uint16_t(en >> 16);
+                *reinterpret_cast<uint16_t*>(As + ent_offset<NB>(en)) = uint16_t(en >> 16);
             }
             // every lane makes its writes visible to the tensor core's (async) reads, the warp
             // barrier orders them before lane 0's arrival, which releases them to the MMA issuer
@@ -342,10 +355,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         // A B load that was issued must land before the CTA exits (normally the MMA warp has
         // awaited it already and this returns at once).
         if (kTma && lane == 0 && last_use >= 0) mbar_wait_bounded(&full_b[s], uint32_t(last_use) & 1u);
-    } else if (warp == kMmaWarp) {
+    } else if (warp == S::kMmaWarp) {
         // ---- MMA issuer: the tile sequence in order, one accumulator per band -----------------
         if (lane == 0) {
-            constexpr uint32_t kIdesc = idesc_f16_f32(kBandRows, kSlab, true);
             uint32_t q = 0, u = 0;  // sequence position; bands with tiles so far
             int last_stage = -1;
             uint32_t last_par = 0;
@@ -361,21 +373,24 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     }
                     tc_fence_after();
                     for (int t = 0; t < r.nt; ++t, ++q) {
-                        const int s = int(q % kStages);
-                        const uint32_t par = (q / kStages) & 1u;
+                        const int s = int(q % S::kStages);
+                        const uint32_t par = (q / S::kStages) & 1u;
                         if (!wait_or_abort(&full_a[s], par, abort_flag) ||
                             (kTma && !wait_or_abort(&full_b[s], par, abort_flag))) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t a_addr = smem_u32(smem + s * kStageBytes + kBBytes);
-                        const uint32_t b_addr = smem_u32(smem + s * kStageBytes);
+                        const uint32_t a_addr = smem_u32(smem + s * S::kStageBytes + kBBytes);
+                        const uint32_t b_addr = smem_u32(smem + s * S::kStageBytes);
 #pragma unroll
-                        for (int kk = 0; kk < kBandK / 16; ++kk)
-                            tc_mma_f16(tmem + acc * kSlab, smem_desc(a_addr + kk * 256, 128, kBandK * 16, 0),
-                                       smem_desc(b_addr + kk * 2048, kPanelBytes, 1024, 2), kIdesc,
-                                       (t > 0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < kBandK / 16; ++kk) {
+                            // the band's entries: K-major, unswizzled core matrices; the B tile:
+                            // MN-major, 128-byte swizzle, 64-column panels kPanelBytes apart
+                            const uint64_t da = smem_desc(a_addr + kk * 256, 128, kBandK * 16, 0);
+                            const uint64_t db = smem_desc(b_addr + kk * 2048, kPanelBytes, 1024, 2);
+                            tc_mma_f16(tmem + acc * NB, db, da, S::kIdesc, (t > 0 || kk > 0) ? 1u : 0u);
+                        }
                         tc_commit(&done[s]);
                         last_stage = s;
                         last_par = par;
@@ -391,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         __syncwarp();
     } else {
-        // ---- epilogue: rows 32 q .. 32 q + 31 of each band, q = warp % 4 ------------------------
+        // ---- epilogue ---------------------------------------------------------------------------
         const int quarter = warp & 3;
         const uint32_t lane_base = uint32_t(quarter * 32) << 16;
         uint32_t u = 0;
@@ -403,61 +418,36 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             const int ncols = min(kSlab, O - k0);
             const int row0 = band * P.band_rows;
             const int row_end = min(P.M, row0 + P.band_rows);
-            const int grow = row0 + quarter * 32 + lane;
-            float* crow = C + int64_t(grow) * ldc + k0;
+            // columns k0 + 32 q .. k0 + 32 q + 31 of the band's rows: lane = column
+            const int col = quarter * 32 + lane;
+            const bool col_ok = col < ncols;
+            float* ccol = C + k0 + col;
             if (r.nt == 0) {
-                if (!kAcc && grow < row_end)
-                    for (int c = 0; c < ncols; ++c) crow[c] = 0.f;
+                if (!kAcc && col_ok)
+                    for (int row = row0; row < row_end; ++row) ccol[int64_t(row) * ldc] = 0.f;
             } else {
                 const uint32_t acc = u % kAccs;
                 if (!__all_sync(0xffffffffu, wait_or_abort(&acc_full[acc], (u / kAccs) & 1u, abort_flag))) break;
                 tc_fence_after();
-                // 32 rows x 16 columns at a time: TMEM -> registers (thread = row) -> shared
-                // memory -> registers (4 lanes = one 64-byte row segment) -> C, so that a warp
-                // store writes 8 rows' segments of two whole 32-byte sectors each
-                float* stage_c = reinterpret_cast<float*>(smem + kEpiOffset + quarter * kEpiBytes);
-                const int nrows = min(32, row_end - (row0 + quarter * 32));  // may be <= 0
-                const int sw_w = (lane >> 1) & 3;  // this lane's row swizzle (row = lane)
+                if (quarter * 32 < ncols) {  // warp-uniform: this quarter holds columns < O
 #pragma unroll 1
-                for (int c = 0; c < kSlab; c += kEpiCols) {
-                    if (c >= ncols) break;
-                    uint32_t v[kEpiCols];
-                    tmem_ld_32x32b_x16(tmem + lane_base + acc * kSlab + uint32_t(c), v);
-                    tmem_wait_ld();
+                    for (int rr = 0; rr < NB && row0 + rr < row_end; rr += 16) {
+                        uint32_t v[16];
+                        tmem_ld_32x32b_x16(tmem + lane_base + acc * NB + uint32_t(rr), v);
+                        tmem_wait_ld();
+                        if (col_ok) {
 #pragma unroll
-                    for (int j = 0; j < kEpiCols / 4; ++j)
-                        *reinterpret_cast<float4*>(stage_c + lane * kEpiCols + 4 * (j ^ sw_w)) =
-                            make_float4(__uint_as_float(v[4 * j]) * P.scale, __uint_as_float(v[4 * j + 1]) * P.scale,
-                                        __uint_as_float(v[4 * j + 2]) * P.scale,
-                                        __uint_as_float(v[4 * j + 3]) * P.scale);
-                    __syncwarp();
-                    const int cj = lane & 3;  // this lane's 4-column chunk of a row segment
-                    const int col = c + 4 * cj;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int rr = 8 * i + (lane >> 2);
-                        if (rr < nrows) {
-                            float4 x = *reinterpret_cast<const float4*>(stage_c + rr * kEpiCols +
-                                                                        4 * (cj ^ ((rr >> 1) & 3)));
-                            float* dst = C + int64_t(row0 + quarter * 32 + rr) * ldc + k0 + col;
-                            if (vec_c && col + 3 < ncols) {
-                                if constexpr (kAcc) {
-                                    const float4 o = *reinterpret_cast<const float4*>(dst);
-                                    x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+                            for (int j = 0; j < 16; ++j) {
+                                const int row = row0 + rr + j;
+                                if (row < row_end) {
+                                    float* dst = ccol + int64_t(row) * ldc;
+                                    float x = __uint_as_float(v[j]) * P.scale;
+                                    if constexpr (kAcc) x += *dst;
+                                    __stcs(dst, x);
                                 }
-                                __stcs(reinterpret_cast<float4*>(dst), x);
-                            } else {
-                                const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                                for (int k = 0; k < 4; ++k)
-                                    if (col + k < ncols) {
-                                        if constexpr (kAcc) dst[k] += xs[k];
-                                        else dst[k] = xs[k];
-                                    }
                             }
                         }
                     }
-                    __syncwarp();  // the staging tile is rewritten by the next 16 columns
                 }
                 tc_fence_before();
                 mbar_arrive(&acc_empty[acc]);
@@ -471,33 +461,36 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (tid == 0 && *abort_flag != 0) atomicOr(P.status, kStatusTimeout);
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        tmem_dealloc(tmem, S::kTmemCols);
     }
 }
 
-template <bool kTma, bool kAcc, typename BT>
+template <bool kTma, bool kAcc, typename BT, int NB>
 cudaError_t launch_band_t(const BandPlanView& P, const CUtensorMap& tmap, const BT* B, int64_t ldb, int O, float* C,
                           int64_t ldc, cudaStream_t st) {
-    auto kern = vcsr_band_kernel<kTma, kAcc, BT>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    using S = BandShape<NB>;
+    auto kern = vcsr_band_kernel<kTma, kAcc, BT, NB>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
     if (e != cudaSuccess) return e;
     int dev = 0, sms = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    const int vec_c = ((ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) ? 1 : 0;
     const int64_t items = int64_t(P.n_bands) * ((O + kSlab - 1) / kSlab);
     if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
-    // persistent: at most kCtasPerSm CTAs per SM, each walking its items in a strided order
-    const int grid = int(std::min<int64_t>(items, int64_t(sms) * kCtasPerSm));
-    kern<<<grid, kThreads, kSmemBytes, st>>>(P, tmap, B, ldb, O, C, ldc, vec_c);
+    // persistent: at most kCtas CTAs per SM, each walking its items in a strided order
+    const int grid = int(std::min<int64_t>(items, int64_t(sms) * S::kCtas));
+    kern<<<grid, S::kThreads, S::kSmemBytes, st>>>(P, tmap, B, ldb, O, C, ldc);
     return cudaGetLastError();
 }
 
 template <bool kTma, typename BT>
 cudaError_t launch_band_b(const BandPlanView& P, const CUtensorMap& tmap, const BT* B, int64_t ldb, int O, float* C,
                           int64_t ldc, bool accumulate, cudaStream_t st) {
-    return accumulate ? launch_band_t<kTma, true, BT>(P, tmap, B, ldb, O, C, ldc, st)
-                      : launch_band_t<kTma, false, BT>(P, tmap, B, ldb, O, C, ldc, st);
+    if (P.band_rows <= 64)
+        return accumulate ? launch_band_t<kTma, true, BT, 64>(P, tmap, B, ldb, O, C, ldc, st)
+                          : launch_band_t<kTma, false, BT, 64>(P, tmap, B, ldb, O, C, ldc, st);
+    return accumulate ? launch_band_t<kTma, true, BT, 128>(P, tmap, B, ldb, O, C, ldc, st)
+                      : launch_band_t<kTma, false, BT, 128>(P, tmap, B, ldb, O, C, ldc, st);
 }
 
 }  // namespace
@@ -550,7 +543,7 @@ void band_keys(const RowViewHost& rv, int r0, int r1, uint64_t* out) {
 }  // namespace
 
 BandChoice choose_band_sampled(int M, const BandSampleFetch& fetch) {
-    static const int kCandidates[] = {128, 127, 126, 124, 120, 112, 96, 64};
+    static const int kCandidates[] = {128, 127, 126, 124, 120, 112, 96, 64, 62, 60, 56, 48, 32};
     BandChoice best{kBandRows, 0.0};
     if (M <= 0) return best;
     // Up to 64 bands spread over the matrix, for every candidate height.
@@ -588,8 +581,10 @@ BandChoice choose_band_sampled(int M, const BandSampleFetch& fetch) {
             rows += ranges[i].second - ranges[i].first;
             ents += int64_t(cols.size());
         }
-        // tensor-core tiles per row, plus the epilogue of a band (about two tiles' time)
-        const double cost = (double(tiles) + 2.0 * samples) / double(std::max<int64_t>(rows, 1));
+        // tensor-core time per row: a tile of a band of at most 64 rows (N = 64) takes 1.85 ns on a
+        // B200, one of a taller band (N = 128) 2.18 ns; plus about half a tile per band
+        const double tile_cost = H <= 64 ? 1.0 : 1.17;
+        const double cost = (double(tiles) * tile_cost + 0.5 * samples) / double(std::max<int64_t>(rows, 1));
         if (H == kCandidates[0] || cost < best_cost * 0.995) {
             best_cost = cost;
             best = BandChoice{H, tiles > 0 ? double(ents) / double(tiles) : 0.0,

@@ -15,7 +15,7 @@ namespace dev {
 #ifndef VCSRMC_BAND_K
 #define VCSRMC_BAND_K 64
 #endif
-constexpr int kBandRows = 128;          // rows per band at most = tcgen05 tile M
+constexpr int kBandRows = 128;          // rows per band at most = the largest MMA N
 constexpr int kBandK = VCSRMC_BAND_K;   // columns of A (= rows of B) per tile: kBandK / 16 MMA K steps
 constexpr int kBandColBits = kBandK == 64 ? 6 : 5;  // bits of an entry's column within its tile
 static_assert(kBandK == 32 || kBandK == 64, "tiles of 32 or 64 columns");
@@ -37,7 +37,8 @@ struct BandViewHost {
     std::vector<uint32_t> ents;
 };
 
-// The band height (<= 128) that minimises tiles per row (plus a per-band cost), estimated on a
+// The band height (<= 128) that minimises the tensor-core time per row (tiles per row, weighted by
+// the MMA size: N = 64 for bands of at most 64 rows, else 128; plus a per-band cost), estimated on a
 // sample of bands, the mean entries per tile it gives, and the fraction of the sampled entries in
 // tiles holding at least kBandMinEntriesPerTile entries (the HYBRID plan's dense part).
 struct BandChoice {
