@@ -325,6 +325,7 @@ void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int6
         P.split_rows = d->split_rows;
         P.n_split_rows = d->n_split_rows;
         P.M = d->M;
+        P.N = d->N;
         P.scale = d->scale;
         const int64_t row_bytes = ldb * (b_dtype == VCSRMC_F16 ? 2 : 4);
         ensure_hot_buffer(d, row_bytes, st);
@@ -366,6 +367,7 @@ void launch_spmm(const vcsrmc_device_format* d, const void* B, int b_dtype, int6
             R.split_rows = d->hr_split;
             R.n_split_rows = d->hr_n_split;
             R.M = d->M;
+            R.N = d->N;
             R.scale = d->scale;
             e = dev::spmm_rows(R, B, b_dtype == VCSRMC_F16 ? 1 : 0, ldb, O, C, ldc, true, st);
             cuda_check(e, "SpMM launch (hybrid plan, rows part)");

@@ -193,11 +193,11 @@ static_assert(kInFlight == 8 || kInFlight == 16, "a batch of 16 entries in round
 
 // A lane group (kL lanes: 16 for fp16 B, 32 for fp32 B) owns one work unit and one 128-column
 // slab of C; lane sl of the group holds columns c0 .. c0+kE-1 of it. Per batch of kL entries the
-// group stages (column, A value) in shared memory (one 8-byte broadcast read per entry later),
+// group stages (B row offset, A value) in shared memory (one broadcast read per entry later),
 // pads the batch past the unit's end with (column 0, value 0) so no bounds tests are needed,
 // and gathers B eight entries at a time; runs of eight entries without a row end skip the
 // per-entry row-end test.
-template <bool kVec, bool kAccumulate, typename VT, typename BT>
+template <bool kVec, bool kAccumulate, typename VT, typename BT, bool kRec16>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks)
     vcsr_rows_kernel(const int4* __restrict__ units, int64_t n_units, const int* __restrict__ rp,
                      const int* __restrict__ cols, const VT* __restrict__ vals, const BT* __restrict__ B,
@@ -212,6 +212,14 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks
     const int sub = lane / kL, sl = lane % kL;
     const unsigned gmask = kL == 32 ? kFull : (0xffffu << (16 * sub));
     Staged* stage = stage_all + (threadIdx.x >> 5) * 32 + sub * kL;
+    // fp32 B: an entry is staged as 8 bytes (its B row's offset in 16-byte units, or its column on
+    // the element-wise path; A value bits), entry j of lane group g in slot j * kGroups + g, unless
+    // the layout needs the 16-byte records (kRec16: hot columns, or B row offsets past 2^32 16-byte
+    // units). Config 4, fp32 B: 14.43 / 14.83 against 14.79 / 15.28 ms with 16-byte records (two boxes). With fp16 B the
+    // 64-register build then spills, and the 16-byte records stay faster (8.94-9.07 against
+    // 9.31-9.38 ms).
+    constexpr bool kCompact = !kRec16 && sizeof(BT) == 4;
+    uint2* rec = reinterpret_cast<uint2*>(stage_all + (threadIdx.x >> 5) * 32) + sub;
     const int64_t unit = (int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5)) * kGroups + sub;
     if (unit >= n_units) return;  // the whole group leaves together
     const int4 u = units[unit];
@@ -249,7 +257,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks
     }
     for (int q = pb; q < pe; q += kL) {
         const int n = min(kL, pe - q);
-        stage[sl] = Staged{entry_offset(mc, row_bytes, hot_cols, k_copy, hot_delta), mv, uint32_t(cold_hint & (mc >= 0))};
+        if constexpr (!kCompact)
+            stage[sl] = Staged{entry_offset(mc, row_bytes, hot_cols, k_copy, hot_delta), mv, uint32_t(cold_hint & (mc >= 0))};
+        else
+            rec[sl * kGroups] = make_uint2(kVec ? uint32_t(mc) * uint32_t(row_bytes >> 4) : uint32_t(mc), mv);
         mc = 0;
         mv = 0;
         if (q + kL + sl < pe) {
@@ -277,16 +288,28 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks
             uint32_t av[kInFlight];  // held only when RowsShape<BT>::kReloadA is false
 #pragma unroll
             for (int k = 0; k < kInFlight; ++k) {
-                const Staged e = stage[j + k];
-                if constexpr (!RowsShape<BT>::kReloadA) av[k] = e.v;
-                const BT* p = reinterpret_cast<const BT*>(bbase + e.off);
-                raw[k] = e.once ? load16_once<kVec>(p, nv) : load16<kVec>(p, nv);
+                if constexpr (!kCompact) {
+                    const Staged e = stage[j + k];
+                    if constexpr (!RowsShape<BT>::kReloadA) av[k] = e.v;
+                    const BT* p = reinterpret_cast<const BT*>(bbase + e.off);
+                    raw[k] = e.once ? load16_once<kVec>(p, nv) : load16<kVec>(p, nv);
+                } else {
+                    const uint32_t c = reinterpret_cast<const uint32_t*>(rec + (j + k) * kGroups)[0];
+                    if constexpr (!RowsShape<BT>::kReloadA) av[k] = rec[(j + k) * kGroups].y;
+                    const BT* p = reinterpret_cast<const BT*>(kVec ? bbase + size_t(c) * 16u
+                                                                   : bbase + (long long)int(c) * row_bytes);
+                    raw[k] = load16<kVec>(p, nv);
+                }
             }
             // A value of entry j + k at its FMA: from shared memory (8 registers fewer held while the
             // gathers are in flight) or from the registers loaded with the gathers
             auto a_of = [&](int k) -> uint32_t {
-                if constexpr (RowsShape<BT>::kReloadA) return stage[j + k].v;
-                else return av[k];
+                if constexpr (RowsShape<BT>::kReloadA) {
+                    if constexpr (!kCompact) return stage[j + k].v;
+                    else return rec[(j + k) * kGroups].y;
+                } else {
+                    return av[k];
+                }
             };
             const unsigned eb = (ends >> j) & ((1u << kInFlight) - 1u);
             if (eb == 0) {
@@ -559,8 +582,14 @@ cudaError_t launch_rows_t(const RowPlanView& P, const BT* B, int64_t ldb, int O,
     }
     LaunchShape L(dim3(unsigned(blocks), unsigned((O + 127) / 128)), dim3(kWarpsPerBlock * 32), st, window,
                   window_bytes);
-    return cudaLaunchKernelEx(&L.cfg, vcsr_rows_kernel<kVec, kAcc, VT, BT>, P.units, P.n_units, P.rp, P.cols, vals, B,
-                              row_bytes, O, C, ldc, P.scale, hot_cols, k_copy, hot_delta, cold_hint);
+    // 16-byte records: hot columns (ranked entries), or B too large for 32-bit row offsets in
+    // 16-byte units (kVec) or for int32 columns times the pitch (element-wise path)
+    const bool rec16 = P.hot.n_hot > 0 || int64_t(P.N) * (kVec ? row_bytes / 16 : 1) > 0xffffffffLL;
+    if (rec16)
+        return cudaLaunchKernelEx(&L.cfg, vcsr_rows_kernel<kVec, kAcc, VT, BT, true>, P.units, P.n_units, P.rp, P.cols,
+                                  vals, B, row_bytes, O, C, ldc, P.scale, hot_cols, k_copy, hot_delta, cold_hint);
+    return cudaLaunchKernelEx(&L.cfg, vcsr_rows_kernel<kVec, kAcc, VT, BT, false>, P.units, P.n_units, P.rp, P.cols,
+                              vals, B, row_bytes, O, C, ldc, P.scale, hot_cols, k_copy, hot_delta, cold_hint);
 }
 
 template <typename VT, typename BT>

@@ -62,6 +62,7 @@ struct RowPlanView {
     const int* split_rows;
     int n_split_rows;
     int M;
+    int N = 0;  // columns of A (rows of B): bounds the B row offsets the kernel forms
     float scale;
     RowHotView hot;
 };
