@@ -215,9 +215,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks
     // fp32 B: an entry is staged as 8 bytes (its B row's offset in 16-byte units, or its column on
     // the element-wise path; A value bits), entry j of lane group g in slot j * kGroups + g, unless
     // the layout needs the 16-byte records (kRec16: hot columns, or B row offsets past 2^32 16-byte
-    // units). Config 4, fp32 B: 14.43 / 14.83 against 14.79 / 15.28 ms with 16-byte records (two boxes). With fp16 B the
-    // 64-register build then spills, and the 16-byte records stay faster (8.94-9.07 against
-    // 9.31-9.38 ms).
+    // units). Config 4, fp32 B: 14.43 / 14.83 against 14.79 / 15.28 ms with 16-byte records (two
+    // boxes). With fp16 B the 64-register build then spills, and the 16-byte records stay faster
+    // (8.94-9.07 against 9.31-9.38 ms).
     constexpr bool kCompact = !kRec16 && sizeof(BT) == 4;
     uint2* rec = reinterpret_cast<uint2*>(stage_all + (threadIdx.x >> 5) * 32) + sub;
     const int64_t unit = (int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5)) * kGroups + sub;
