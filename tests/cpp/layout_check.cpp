@@ -316,7 +316,7 @@ int main() {
         rv.cols = a.col;
         rv.vals = a.val;
         const BandChoice c = choose_band(rv, a.M);
-        const std::set<int> cand = {128, 127, 126, 124, 120, 112, 96, 64};
+        const std::set<int> cand = {128, 127, 126, 124, 120, 112, 96, 64, 62, 60, 56, 48, 32};
         expect(cand.count(c.band_rows) == 1, "chosen band height is a candidate", c.band_rows, 0);
         expect(a.col.empty() || c.entries_per_tile >= 1.0, "entries per tile", trial, 0);
     }
