@@ -22,6 +22,7 @@
 #include "cuda/plan_band.hpp"
 #include "cuda/plan_rows.hpp"
 #include "vcsrmc/csr.hpp"
+#include "vcsrmc/gen.hpp"
 #include "vcsrmc/vcsr_formats.hpp"
 
 using namespace vcsrmc::dev;
@@ -323,11 +324,25 @@ int main() {
     Csr empty;  // M = 0
     empty.rp = {0};
     check_band(empty, 128);
+    // The 27-point stencil on 100^3: at 62-row bands each of a band's 9 column windows is exactly 64
+    // columns wide (one tile each) and runs at MMA N = 64, which the chooser must prefer.
+    int stencil_rows = 0;
+    {
+        const vcsrmc::CSR st = vcsrmc::gen_stencil27(100, 100, 100, 0);
+        RowViewHost rv;
+        rv.rp = st.row_ptr;
+        rv.cols = st.col;
+        rv.vals = st.val;
+        const BandChoice c = choose_band(rv, st.M);
+        stencil_rows = c.band_rows;
+        expect(c.band_rows == 62, "stencil band height", c.band_rows, 62);
+        expect(c.entries_per_tile > 150.0, "stencil entries per tile", int(c.entries_per_tile), 150);
+    }
     if (failures) {
         std::printf("%d checks failed\n", failures);
         return 1;
     }
-    std::printf("OK unit_sets=%lld band_views=%lld row_views=%lld tile_width=%d densest_tile=%lld\n", n_units_checked,
-                n_bands_checked, n_row_views, kBandK, densest_tile);
+    std::printf("OK unit_sets=%lld band_views=%lld row_views=%lld tile_width=%d densest_tile=%lld stencil_band=%d\n",
+                n_units_checked, n_bands_checked, n_row_views, kBandK, densest_tile, stencil_rows);
     return 0;
 }

@@ -31,3 +31,4 @@ def test_host_layout_builders(tmp_path):
     fields = dict(kv.split("=") for kv in out.stdout.split()[1:])
     assert int(fields["row_views"]) > 0
     assert int(fields["densest_tile"]) > 256  # tiles beyond the producers' register window are covered
+    assert int(fields["stencil_band"]) == 62  # the 100^3 stencil's windows fill 64-column tiles exactly
