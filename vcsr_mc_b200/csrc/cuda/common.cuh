@@ -93,12 +93,6 @@ __device__ __forceinline__ void tma_gather4_2d(void* smem_dst, const void* tmap,
           "r"(y1), "r"(y2), "r"(y3)
         : "memory");
 }
-// Brings a 2-D box of the tensor into L2 (no shared memory, no completion to wait for).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int x, int y) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
-                 ::"l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y)
-                 : "memory");
-}
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
