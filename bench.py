@@ -350,7 +350,7 @@ def main() -> None:
     ap.add_argument("--segw", type=int, default=32)
     ap.add_argument("--tileK", type=int, default=128)
     ap.add_argument("--plan", choices=["rows", "segment", "band", "hybrid"], default="rows")
-    ap.add_argument("--e2e-steps", type=int, default=12)
+    ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true")
