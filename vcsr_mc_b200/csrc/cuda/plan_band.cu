@@ -15,13 +15,13 @@
 //     shared-memory stages (B 16 KB + A NB x 128 bytes each). Producer warp w owns stage w: once
 //     the MMAs of its previous tile have completed it starts the TMA load of its next B tile,
 //     clears its previous entries from the A tile (the positions it remembers, or the whole tile
-//     after a large one), writes the new entries and arrives on the stage's barrier. Its registers run one position ahead (entries and bounds are loaded two
-//     iterations before use);
+//     after a large one), writes the new entries and arrives on the stage's barrier. Its
+//     registers run one position ahead (entries and bounds are loaded two iterations before use);
 //   * lane 0 of the MMA warp issues the MMAs in sequence order into one of two TMEM
 //     accumulators, so the MMAs of a band overlap the epilogue of the previous one;
 //   * four epilogue warps read their TMEM lane quarter (tcgen05.ld: a lane is a column of C, the
-//     registers are rows) and store each row's 32 columns as one 128-byte warp store (read once
-//     for C += A*B).
+//     registers are rows) and store each row's 32 columns as one 128-byte warp store (for
+//     C += A*B, one 128-byte warp reduction).
 // Several CTAs per SM outrun one CTA with more stages (0.300 against 0.365 ms on a 27-point
 // stencil in an earlier form): each CTA's MMA issuer walks its tiles one at a time, and the other
 // CTAs fill its waits. 64-column tiles beat 32-column ones by halving the tiles.
@@ -56,7 +56,8 @@ namespace {
 // Per SM, stages in flight decide the speed (each stage waits for its B tile's TMA load after its
 // previous MMAs complete): on a 27-point stencil at 62-row bands, 2 CTAs x 3 stages took 0.298 ms,
 // 2 x 4 stages 0.278 ms and 3 x 3 stages 0.2665 ms; 128-row bands (2 x 3 stages) 0.289 ms, against
-// 0.294 ms for the same product with a row of C per TMEM lane and a transposing epilogue.
+// 0.294 ms for the same product with a row of C per TMEM lane and a transposing epilogue (all with
+// an L2 prefetch of each stage's next B tile, since dropped: 3 x 3 stages now 0.246 ms).
 constexpr int kSlab = 128;                       // columns of B and C per work item (= MMA M)
 constexpr int kSaved = 8;                        // entries a producer lane keeps per tile (to clear them)
 constexpr int kAccs = 2;                         // TMEM accumulators: one band's MMAs overlap the previous epilogue
@@ -435,9 +436,13 @@ __global__ void __launch_bounds__(BandShape<NB>::kThreads, BandShape<NB>::kCtas)
                                 const int row = row0 + rr + j;
                                 if (row < row_end) {
                                     float* dst = ccol + int64_t(row) * ldc;
-                                    float x = __uint_as_float(v[j]) * P.scale;
-                                    if constexpr (kAcc) x += *dst;
-                                    __stcs(dst, x);
+                                    const float x = __uint_as_float(v[j]) * P.scale;
+                                    // C += A*B: a fire-and-forget reduction (red.global.add.f32) into
+                                    // a row that only this band writes, instead of a load-add-store
+                                    // that waits for the old value row by row (config 3: 1.136 ms
+                                    // with the loads, against 0.246 ms for C = A*B)
+                                    if constexpr (kAcc) atomicAdd(dst, x);
+                                    else __stcs(dst, x);
                                 }
                             }
                         }
