@@ -258,7 +258,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks
     for (int q = pb; q < pe; q += kL) {
         const int n = min(kL, pe - q);
         if constexpr (!kCompact)
-            stage[sl] = Staged{entry_offset(mc, row_bytes, hot_cols, k_copy, hot_delta), mv, uint32_t(cold_hint & (mc >= 0))};
+            stage[sl] = kRec16 ? Staged{entry_offset(mc, row_bytes, hot_cols, k_copy, hot_delta), mv,
+                                        uint32_t(cold_hint & (mc >= 0))}
+                               : Staged{(long long)mc * row_bytes, mv, 0u};
         else
             rec[sl * kGroups] = make_uint2(kVec ? uint32_t(mc) * uint32_t(row_bytes >> 4) : uint32_t(mc), mv);
         mc = 0;
@@ -292,7 +294,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, RowsShape<BT>::kMinBlocks
                     const Staged e = stage[j + k];
                     if constexpr (!RowsShape<BT>::kReloadA) av[k] = e.v;
                     const BT* p = reinterpret_cast<const BT*>(bbase + e.off);
-                    raw[k] = e.once ? load16_once<kVec>(p, nv) : load16<kVec>(p, nv);
+                    // the evict-first flag is read only where hot columns can set it (config 4,
+                    // fp16 B: 9.00 against 9.30-9.38 ms with the flag read for every entry)
+                    if constexpr (kRec16) raw[k] = e.once ? load16_once<kVec>(p, nv) : load16<kVec>(p, nv);
+                    else raw[k] = load16<kVec>(p, nv);
                 } else {
                     const uint32_t c = reinterpret_cast<const uint32_t*>(rec + (j + k) * kGroups)[0];
                     if constexpr (!RowsShape<BT>::kReloadA) av[k] = rec[(j + k) * kGroups].y;
