@@ -128,7 +128,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
@@ -137,20 +137,32 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
-    def stop(self) -> dict:
+    def stop(self, window=None) -> dict:
+        """Summary of the samples taken in window = (t0, t1) (wall-clock seconds around the timed
+        region), or of all samples when none fall inside it."""
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0,
+                    "timed_region_only": False}
         time.sleep(0.25)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
+        return summarize_clock_samples(self.lines, window)
+
+
+CLOCK_REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+def summarize_clock_samples(lines, window=None) -> dict:
+    """lines: (arrival time, one nvidia-smi csv line of ClockSampler.QUERY). A line arrives after it
+    was taken, so the window is widened by 0.1 s (two sampling intervals) at its end."""
+    def parse(sel):
         sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for _, ln in sel:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -159,11 +171,18 @@ class ClockSampler:
                 smax.append(float(f[2]))
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            for n, v in zip(CLOCK_REASONS, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return sm, smax, reasons
+
+    in_window = window is not None
+    sm, smax, reasons = parse([x for x in lines if window[0] <= x[0] <= window[1] + 0.1] if in_window else lines)
+    if in_window and not sm:  # a timed region shorter than one interval: every sample
+        in_window = False
+        sm, smax, reasons = parse(lines)
+    return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+            "reasons": sorted(reasons), "samples": len(sm), "timed_region_only": in_window}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -526,6 +545,7 @@ def main() -> None:
     time.sleep(0.3)
     barrier()
     torch.cuda.synchronize()
+    tw0 = time.time()
     start.record(stream)
     for i in range(args.steps):
         # per-step events only where something else runs between the SpMM calls (the L2 flush, or
@@ -537,8 +557,9 @@ def main() -> None:
             step(i=i)
     stop.record(stream)
     torch.cuda.synchronize()
+    tw1 = time.time()
     barrier()
-    clk = clocks.stop()
+    clk = clocks.stop(window=(tw0, tw1))
     total_ms = start.elapsed_time(stop)
     kern_ms = float(np.mean([a.elapsed_time(b) for a, b in kev])) if per_step_events else total_ms / args.steps
     status = dV.status()
@@ -795,6 +816,7 @@ def main() -> None:
                        "format_build": args.build, "format_build_upload_s": build_s,
                        "rows_unit_nnz": info["rows_unit_nnz"], "band_rows": info["band_rows"],
                        "band_tiles": info["n_tiles"], "clock_samples": clk["samples"],
+                       "clock_samples_timed_region_only": clk["timed_region_only"],
                        "hot_columns": {**hot, "n_hot": info["n_hot"]}},
         }
         emit(line)
