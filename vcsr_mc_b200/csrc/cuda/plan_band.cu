@@ -440,7 +440,7 @@ __global__ void __launch_bounds__(BandShape<NB>::kThreads, BandShape<NB>::kCtas)
                                     // C += A*B: a fire-and-forget reduction (red.global.add.f32) into
                                     // a row that only this band writes, instead of a load-add-store
                                     // that waits for the old value row by row (config 3: 1.136 ms
-                                    // with the loads, against 0.246 ms for C = A*B)
+                                    // with the loads, 0.244 ms with the reductions)
                                     if constexpr (kAcc) atomicAdd(dst, x);
                                     else __stcs(dst, x);
                                 }
